@@ -1,0 +1,473 @@
+"""Benchmark of the paged KV-cache transfer path on B200.
+
+One step = store every chunk of the workload's token sequence from the paged
+KV cache into its LMCache object (multi_layer_kv_transfer, direction=True),
+then retrieve every chunk back (direction=False): the data-parallel hot path
+of LMCache's GPU connector (VLLMPagedMemGPUConnectorV2.from_gpu / to_gpu).
+
+  value  KV payload GB/s (both directions; skipped slots excluded) with the
+         LMCache objects in HBM, inputs resident before the timed region.
+  e2e    the same metric with the LMCache objects in pinned host memory (the
+         deployment case: zero-copy PCIe writes on store, reads on retrieve),
+         called through c_ops with each chunk's slot mapping copied from
+         pinned host memory inside the timed region.
+
+Default workload c2 (Llama-3-8B: 32 layers, 8 x 128 heads, block_size 16,
+8192 blocks per layer, 8192 tokens in 32 chunks of 256). Multi-GPU: one
+process per GPU (torchrun); each rank moves its own KV shard with its own
+seed; no collective is on the data path (gloo only for the start barrier and
+the max-over-ranks timing).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2]
+  python bench.py --impl reference    # CPU path of the reference semantics
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "lmcache-ascend_b200"))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "KV store/retrieve GB/s (HBM & pinned-host MemoryObj)"
+UNIT = "GB/s"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="c2")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=None,
+                    help="timed steps of the pinned-host leg (default: --steps)")
+    ap.add_argument("--cpu-budget", type=float, default=15.0,
+                    help="seconds of CPU work for the CPU baseline sample")
+    ap.add_argument("--cpu-max-blocks", type=int, default=1024,
+                    help="paged blocks per layer of the host-resident CPU baseline buffers")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--blocks", type=int, default=None,
+                    help="override paged blocks per layer (small profiling cases only)")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# process group / clocks
+# ---------------------------------------------------------------------------
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=300))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict:
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                maxes.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes),
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+def measured_peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    except (OSError, KeyError, ValueError):
+        return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def committed_traffic(kernel: str, workload: str):
+    """dram read+write bytes per launch from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", f"{kernel}_{workload}.md")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return float(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+
+def run_ours(args):
+    rank, world, local = dist_setup()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+
+    from lmcache_b200 import c_ops
+    from lmcache_b200 import workloads as wl
+    from lmcache_b200.v1.memory_management import PinMemoryAllocator
+
+    spec = wl.SPECS[args.workload]
+    if args.blocks:
+        import dataclasses
+
+        spec = dataclasses.replace(spec, num_blocks=args.blocks)
+    seed = rank
+    caches = wl.make_kv_caches(spec, dev, seed=seed)
+    ptrs = wl.pointer_tensor(caches, dev)
+    slots = wl.make_slot_mapping(spec, seed=seed)
+    host_chunks = [c.contiguous().pin_memory() for c in wl.chunks(slots, spec.chunk_size)]
+    dev_chunks = [c.to(dev) for c in host_chunks]
+    n_chunks = len(dev_chunks)
+    pbs = 0 if spec.use_mla else spec.page_buffer_size
+    payload = wl.payload_bytes(spec, slots)  # one direction, whole sequence
+    step_payload = 2 * payload
+    hbm_objs = [torch.empty(spec.memobj_shape(len(c)), dtype=torch.bfloat16, device=dev)
+                for c in dev_chunks]
+    stream = torch.cuda.current_stream()
+
+    def step_hbm(events=None):
+        for i in range(n_chunks):
+            if events is not None:
+                events[0][i].record(stream)
+            c_ops.multi_layer_kv_transfer(hbm_objs[i], ptrs, dev_chunks[i], dev, pbs, True,
+                                          spec.use_mla)
+            if events is not None:
+                events[1][i].record(stream)
+        for i in range(n_chunks):
+            if events is not None:
+                events[2][i].record(stream)
+            c_ops.multi_layer_kv_transfer(hbm_objs[i], ptrs, dev_chunks[i], dev, pbs, False,
+                                          spec.use_mla)
+            if events is not None:
+                events[3][i].record(stream)
+
+    # ---- value: HBM-resident objects -------------------------------------
+    for _ in range(args.warmup):
+        step_hbm()
+    torch.cuda.synchronize()
+    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(n_chunks)] for _ in range(4)]
+          for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for k in range(args.steps):
+            step_hbm(ev[k])
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    t_ms = max_over_ranks(start.elapsed_time(end), world)
+    total_payload = sum_over_ranks(step_payload * args.steps, world)
+    value = total_payload / (t_ms / 1e3) / 1e9
+    store_ms = [ev[k][0][i].elapsed_time(ev[k][1][i]) for k in range(args.steps)
+                for i in range(n_chunks)]
+    retr_ms = [ev[k][2][i].elapsed_time(ev[k][3][i]) for k in range(args.steps)
+               for i in range(n_chunks)]
+    n_valid = [int((c >= 0).sum()) for c in host_chunks]
+    launch_payload = [n * spec.num_layers * spec.kv * spec.hidden * 2 for n in n_valid]
+    # Algorithmic HBM bytes per launch: payload read + written, slot ids, layer pointers.
+    alg = [2 * p + len(c) * 8 + spec.num_layers * 8 for p, c in zip(launch_payload, host_chunks)]
+    alg_total = sum(alg) * 2 * args.steps
+    kern_s = (sum(store_ms) + sum(retr_ms)) / 1e3
+    achieved = alg_total / kern_s / 1e9
+    peaks = measured_peaks()
+    avg_launch_ms = (sum(store_ms) + sum(retr_ms)) / len(store_ms + retr_ms)
+    avg_alg = sum(alg) / len(alg)
+    clock_summary = clocks.summary()
+
+    # ---- e2e: pinned-host objects through c_ops ------------------------
+    obj_bytes = sum(torch.Size(spec.memobj_shape(len(c))).numel() * 2 for c in dev_chunks)
+    arena = PinMemoryAllocator(obj_bytes + 256 * n_chunks + (1 << 20))
+    host_objs = [arena.allocate(spec.memobj_shape(len(c)), torch.bfloat16).tensor
+                 for c in dev_chunks]
+    slot_dev_bufs = [torch.empty_like(c) for c in dev_chunks]
+
+    def step_e2e():
+        for i in range(n_chunks):
+            slot_dev_bufs[i].copy_(host_chunks[i], non_blocking=True)
+            c_ops.multi_layer_kv_transfer(host_objs[i], ptrs, slot_dev_bufs[i], dev, pbs, True,
+                                          spec.use_mla)
+        for i in range(n_chunks):
+            c_ops.multi_layer_kv_transfer(host_objs[i], ptrs, slot_dev_bufs[i], dev, pbs, False,
+                                          spec.use_mla)
+
+    e2e_steps = args.e2e_steps or args.steps
+    e2e = {}
+    for mode in ("zerocopy", "dma"):
+        os.environ["LMCB_HOST_RETRIEVE"] = mode
+        for _ in range(max(1, min(args.warmup, 3))):
+            step_e2e()
+        torch.cuda.synchronize()
+        barrier(world)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(e2e_steps):
+            step_e2e()
+        s1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        ms = max_over_ranks(s0.elapsed_time(s1), world)
+        e2e[mode] = sum_over_ranks(step_payload * e2e_steps, world) / (ms / 1e3) / 1e9
+    os.environ.pop("LMCB_HOST_RETRIEVE", None)
+    # Separate store / retrieve pinned-host rates (zero-copy store; both retrieve paths).
+    dir_rates = {}
+    for label, direction, mode in (("store_zerocopy", True, "zerocopy"),
+                                   ("retrieve_zerocopy", False, "zerocopy"),
+                                   ("retrieve_dma", False, "dma")):
+        os.environ["LMCB_HOST_RETRIEVE"] = mode
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(2):
+            for i in range(n_chunks):
+                c_ops.multi_layer_kv_transfer(host_objs[i], ptrs, dev_chunks[i], dev, pbs,
+                                              direction, spec.use_mla)
+        s1.record(stream)
+        torch.cuda.synchronize()
+        dir_rates[label] = round(2 * payload / (s0.elapsed_time(s1) / 1e3) / 1e9, 2)
+    os.environ.pop("LMCB_HOST_RETRIEVE", None)
+    best_mode = max(e2e, key=e2e.get)
+
+    # ---- CPU baseline (rank 0, N = 1) -----------------------------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle.cpu_baseline import CpuTransfer
+
+        ct = CpuTransfer(spec, max_blocks=args.cpu_max_blocks, seed=0)
+        m = ct.measure(args.cpu_budget)
+        cpu = {
+            "value": round(m["gbps"], 3),
+            "unit": UNIT,
+            "cores": m["threads"],
+            "kind": "port",
+            "sample": (f"torch index_select/index_copy_ store+retrieve of {m['chunks_per_step']} "
+                       f"of {n_chunks} chunks x {m['steps']} steps ({m['seconds']:.1f} s), "
+                       f"{spec.name} per-chunk shapes, paged buffers reduced to "
+                       f"{m['blocks_per_layer']} of {m['full_blocks_per_layer']} blocks/layer "
+                       f"in host RAM"),
+        }
+
+    if rank == 0:
+        traffic = committed_traffic("transfer_rows_kernel", spec.name)
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(t_ms / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) bf16 KV, seeded random block slot mappings)",
+            "config": {
+                "workload": f"{spec.name}: {spec.description}",
+                "num_layers": spec.num_layers,
+                "kv_heads": spec.num_heads,
+                "head_dim": spec.head_size,
+                "block_size": spec.block_size,
+                "blocks_per_layer": spec.num_blocks,
+                "tokens": spec.num_tokens,
+                "chunk_tokens": spec.chunk_size,
+                "step": "store all chunks then retrieve all chunks (multi_layer_kv_transfer)",
+                "payload_bytes_per_step_per_gpu": step_payload,
+                "l2": "inputs larger than L2 (each step touches 2x payload of distinct "
+                      "paged rows and LMCache objects, >126 MB)",
+                "parallelism": f"{world} independent ranks (per-rank KV shard), no collective",
+            },
+            "e2e": {
+                "value": round(e2e[best_mode], 2),
+                "unit": UNIT,
+                "h2d_bytes_per_step": payload + sum(c.numel() * 8 for c in host_chunks),
+                "d2h_bytes_per_step": payload,
+                "path": f"pinned-host MemoryObj via c_ops; store zero-copy, retrieve {best_mode}",
+                "by_retrieve_path": {k: round(v, 2) for k, v in e2e.items()},
+                "per_direction_gbs": dir_rates,
+            },
+            "roofline": {
+                "bound": "hbm",
+                "kernel": "transfer_rows_kernel",
+                "achieved": round(achieved, 1),
+                "peak": peaks["hbm_gbs"],
+                "peak_source": peaks["source"],
+                "unit": "GB/s",
+                "frac": round(achieved / peaks["hbm_gbs"], 4),
+                "traffic": traffic,
+                "algorithmic_bytes_per_launch": round(avg_alg),
+                "avg_launch_us": round(avg_launch_ms * 1e3, 2),
+                "store_avg_us": round(statistics.mean(store_ms) * 1e3, 2),
+                "retrieve_avg_us": round(statistics.mean(retr_ms) * 1e3, 2),
+            },
+            "cpu_baseline": cpu,
+            "gpu_launches": args.steps * 2 * n_chunks,
+            "clocks": clock_summary,
+        }
+        print(json.dumps(line), flush=True)
+    arena.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the reference-semantics CPU path on the host cores
+# ---------------------------------------------------------------------------
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    from lmcache_b200 import workloads as wl
+    from oracle.cpu_baseline import CpuTransfer
+
+    spec = wl.SPECS[args.workload]
+    ct = CpuTransfer(spec, max_blocks=args.cpu_max_blocks, seed=0)
+    # Size one step to about 2 s of CPU work (at most the whole sequence).
+    _, dt = ct.run_step(1)
+    n = max(1, min(len(ct.chunks), int(2.0 / max(dt, 1e-6))))
+    for _ in range(args.warmup):
+        ct.run_step(n)
+    total_b, total_t = 0, 0.0
+    for _ in range(args.steps):
+        b, t = ct.run_step(n)
+        total_b += b
+        total_t += t
+    value = total_b / total_t / 1e9
+    sample = (f"torch index_select/index_copy_ store+retrieve of {n} of {len(ct.chunks)} chunks "
+              f"per step, {spec.name} per-chunk shapes, paged buffers reduced to "
+              f"{ct.spec.num_blocks} of {spec.num_blocks} blocks/layer in host RAM")
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 3),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(total_t / args.steps * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded bf16 KV, seeded random block slot mappings)",
+        "config": {"workload": f"{spec.name}: {spec.description}",
+                   "step": "store then retrieve a bounded sample of chunks on host cores",
+                   "parallelism": "rank 0 only, host threads"},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": ct.threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,72 @@
+// common.cuh -- shared host/device helpers of the lmcache_b200 library.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "lmcache_b200.h"
+
+namespace lmcb {
+
+// Thread-local message of the last failing C-ABI call.
+void set_error(const std::string& msg);
+void clear_error();
+
+// Records `msg` and returns `status` (for `return fail(...)`).
+int fail(int status, const std::string& msg);
+
+// Turns a CUDA error into LMCB_ERR_CUDA with a message naming `what`.
+int cuda_fail(cudaError_t err, const char* what);
+
+#define LMCB_CUDA_TRY(expr)                                  \
+  do {                                                       \
+    cudaError_t lmcb_err_ = (expr);                          \
+    if (lmcb_err_ != cudaSuccess) {                          \
+      return ::lmcb::cuda_fail(lmcb_err_, #expr);            \
+    }                                                        \
+  } while (0)
+
+// Number of SMs of the current device (cached per device).
+int current_sm_count();
+
+// Element size of an lmcb_dtype (0 if unknown).
+int dtype_size(int dtype);
+
+// Device address of the current device's status word (LMCB_DEVICE_FLAG_*
+// bits). Kernels receive it as an argument and set bits with atomicOr; the
+// address is looked up once per device. Returns NULL on failure (and records
+// the error).
+unsigned int* device_status_ptr();
+
+__device__ __forceinline__ void raise_flag(unsigned int* status, unsigned int flag) {
+  atomicOr(status, flag);
+}
+
+// Unsigned division by a loop-invariant divisor with a multiply-high and a
+// shift (the round-up method of Granlund and Montgomery, "Division by
+// invariant integers using multiplication", PLDI 1994). Valid for
+// numerators below 2^31 and divisors in [1, 2^31).
+struct FastDiv {
+  uint32_t d;
+  uint32_t m;
+  uint32_t s;
+
+  __host__ __device__ FastDiv() : d(1), m(0), s(0) {}
+
+  __host__ explicit FastDiv(uint32_t divisor) : d(divisor) {
+    uint32_t l = 0;
+    while ((uint64_t(1) << l) < divisor) ++l;
+    s = l;
+    // m = floor(2^32 * (2^l - d) / d) + 1
+    m = uint32_t(((uint64_t(1) << 32) * ((uint64_t(1) << l) - divisor)) / divisor + 1);
+  }
+
+  __device__ __forceinline__ uint32_t div(uint32_t n) const {
+    uint32_t t = __umulhi(n, m);
+    return (t + n) >> s;
+  }
+};
+
+}  // namespace lmcb

@@ -1,0 +1,481 @@
+// kv_transfer.cu -- paged KV-cache <-> LMCache object row transfer for sm_100a.
+//
+// One kernel core serves every transfer entry point of the reference's c_ops
+// surface (csrc/mem_kernels.cpp): it copies "rows" (one token's hidden_dims
+// elements of K, V or the MLA latent) between vLLM-style paged buffers,
+// addressed through slot ids, and a dense LMCache object. The entry points
+// only differ in how a (kv, layer, slot) triple becomes a paged-side address
+// and a (kv, layer, token) triple becomes an LMCache-side address.
+//
+// Work decomposition: a tile is (kv, layer, TILE consecutive tokens). A CTA
+// takes tiles in a grid-stride loop. For each tile it
+//   1. resolves the tile's rows once: slot id -> paged address, token ->
+//      LMCache address, dropping skipped rows (slot < 0 or out of range) and
+//      compacting the rest into shared memory;
+//   2. moves the surviving rows as a flat array of VEC-byte vectors, UNROLL
+//      independent vectors per thread in flight (all loads, then all stores),
+//      so consecutive threads touch consecutive 16-byte words of a row and
+//      every warp access is fully coalesced, whatever the row length.
+// Rows whose addresses are not VEC-aligned (possible only through the device
+// pointer array, which the host cannot inspect) are copied byte-wise.
+//
+// The same kernel serves HBM and pinned-host (device-mapped, zero-copy)
+// LMCache objects; for host objects every row crosses PCIe exactly once.
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "common.cuh"
+#include "lmcache_b200.h"
+
+namespace lmcb {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kMaxTileRows = 128;
+constexpr int kUnroll = 4;
+constexpr int kTargetTileBytes = 32 * 1024;
+
+// How paged-side row addresses are formed.
+//   kPtrArray: base = ptrs_k[layer] (kv == 0) or ptrs_v[layer] (kv == 1),
+//              plus kv * page_kv_offset.
+//   kDirect:   base = base_k (kv == 0) or base_v (kv == 1).
+enum PagedMode { kPtrArray = 0, kDirect = 1 };
+
+struct TransferParams {
+  // LMCache side: row(kv, layer, t) = lmc + kv*lmc_kv_stride
+  //                                 + layer*lmc_layer_stride + t*lmc_token_stride
+  uint8_t* lmc;
+  int64_t lmc_kv_stride;
+  int64_t lmc_layer_stride;
+  int64_t lmc_token_stride;
+  // Paged side: row(kv, layer, slot) = base(kv, layer) + slot * paged_row_stride
+  const uint64_t* ptrs_k;
+  const uint64_t* ptrs_v;
+  uint8_t* base_k;
+  uint8_t* base_v;
+  int64_t page_kv_offset;
+  int64_t paged_row_stride;
+  int64_t num_paged_rows;  // slot bound; <= 0 means unchecked
+  // Slots and shape.
+  const void* slots;
+  int32_t num_tokens;
+  int32_t num_layers;
+  int32_t num_kv;
+  int32_t tile_rows;       // tokens per tile
+  int32_t tiles_per_seq;   // ceil(num_tokens / tile_rows)
+  int64_t num_tiles;       // num_kv * num_layers * tiles_per_seq
+  int64_t row_bytes;
+  FastDiv row_vecs;        // row_bytes / VEC
+  int32_t page2L;          // 1: paged -> LMCache, 0: LMCache -> paged
+  unsigned int* status;
+};
+
+template <int VEC>
+struct VecType;
+template <> struct VecType<16> { using T = uint4; };
+template <> struct VecType<8> { using T = uint2; };
+template <> struct VecType<4> { using T = uint32_t; };
+template <> struct VecType<2> { using T = uint16_t; };
+
+template <typename SlotT, int VEC, int MODE>
+__global__ void __launch_bounds__(kThreads)
+transfer_rows_kernel(const TransferParams p) {
+  using V = typename VecType<VEC>::T;
+  __shared__ const uint8_t* s_src[kMaxTileRows];
+  __shared__ uint8_t* s_dst[kMaxTileRows];
+  __shared__ int s_warp_count[kMaxTileRows / 32];
+
+  const SlotT* __restrict__ slots = static_cast<const SlotT*>(p.slots);
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+
+  for (int64_t tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+    // tile -> (kv, layer, token range); token tiles vary fastest so
+    // neighbouring CTAs write neighbouring LMCache memory.
+    const int64_t seq = tile / p.tiles_per_seq;
+    const int ttile = static_cast<int>(tile - seq * p.tiles_per_seq);
+    const int kv = static_cast<int>(seq / p.num_layers);
+    const int layer = static_cast<int>(seq - static_cast<int64_t>(kv) * p.num_layers);
+    const int t0 = ttile * p.tile_rows;
+    const int n_tile = min(p.tile_rows, p.num_tokens - t0);
+
+    // ---- 1. resolve and compact the tile's rows -------------------------
+    // Thread r (< n_tile <= kMaxTileRows) resolves token t0 + r.
+    bool valid = false;
+    bool misaligned = false;
+    const uint8_t* src = nullptr;
+    uint8_t* dst = nullptr;
+    if (tid < n_tile) {
+      const int t = t0 + tid;
+      const int64_t slot = static_cast<int64_t>(slots[t]);
+      valid = slot >= 0;
+      if (valid && p.num_paged_rows > 0 && slot >= p.num_paged_rows) {
+        valid = false;
+        raise_flag(p.status, LMCB_DEVICE_FLAG_SLOT_OUT_OF_RANGE);
+      }
+      if (valid) {
+        uint8_t* paged;
+        if (MODE == kPtrArray) {
+          const uint64_t* arr = kv == 0 ? p.ptrs_k : p.ptrs_v;
+          paged = reinterpret_cast<uint8_t*>(arr[layer]) + kv * p.page_kv_offset;
+        } else {
+          paged = kv == 0 ? p.base_k : p.base_v;
+        }
+        paged += slot * p.paged_row_stride;
+        uint8_t* lmc = p.lmc + kv * p.lmc_kv_stride + layer * p.lmc_layer_stride +
+                       static_cast<int64_t>(t) * p.lmc_token_stride;
+        if (p.page2L) {
+          src = paged;
+          dst = lmc;
+        } else {
+          src = lmc;
+          dst = paged;
+        }
+        misaligned = ((reinterpret_cast<uintptr_t>(src) |
+                       reinterpret_cast<uintptr_t>(dst)) & (VEC - 1)) != 0;
+      }
+    }
+    const unsigned ballot = __ballot_sync(0xffffffffu, valid);
+    if (lane == 0 && warp < kMaxTileRows / 32) s_warp_count[warp] = __popc(ballot);
+    const bool mis = __syncthreads_or(misaligned) != 0;  // also publishes the counts
+    if (valid) {
+      int pos = __popc(ballot & ((1u << lane) - 1u));
+      for (int w = 0; w < warp; ++w) pos += s_warp_count[w];
+      s_src[pos] = src;
+      s_dst[pos] = dst;
+    }
+    int n_rows = 0;
+#pragma unroll
+    for (int w = 0; w < kMaxTileRows / 32; ++w) n_rows += s_warp_count[w];
+    __syncthreads();
+
+    // ---- 2. move the rows ------------------------------------------------
+    if (!mis) {
+      const uint32_t rv = p.row_vecs.d;
+      const uint32_t n_items = static_cast<uint32_t>(n_rows) * rv;
+      for (uint32_t base = tid; base < n_items; base += kThreads * kUnroll) {
+        V buf[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          const uint32_t i = base + u * kThreads;
+          if (i < n_items) {
+            const uint32_t r = p.row_vecs.div(i);
+            const uint32_t c = i - r * rv;
+            buf[u] = __ldcs(reinterpret_cast<const V*>(s_src[r]) + c);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          const uint32_t i = base + u * kThreads;
+          if (i < n_items) {
+            const uint32_t r = p.row_vecs.div(i);
+            const uint32_t c = i - r * rv;
+            __stcs(reinterpret_cast<V*>(s_dst[r]) + c, buf[u]);
+          }
+        }
+      }
+    } else {
+      // Byte-wise fallback for rows whose addresses are not VEC-aligned.
+      const int64_t n_bytes = static_cast<int64_t>(n_rows) * p.row_bytes;
+      for (int64_t i = tid; i < n_bytes; i += kThreads) {
+        const int64_t r = i / p.row_bytes;
+        const int64_t c = i - r * p.row_bytes;
+        s_dst[r][c] = s_src[r][c];
+      }
+    }
+    __syncthreads();  // the next tile reuses s_src, s_dst and s_warp_count
+  }
+}
+
+// Largest power of two <= 16 dividing every value in `vals`.
+int pick_vec(std::initializer_list<uint64_t> vals) {
+  uint64_t g = 0;
+  for (uint64_t v : vals) g |= v;
+  if (g % 16 == 0) return 16;
+  if (g % 8 == 0) return 8;
+  if (g % 4 == 0) return 4;
+  if (g % 2 == 0) return 2;
+  return 1;
+}
+
+template <typename SlotT, int VEC>
+cudaError_t launch_vec(const TransferParams& p, int mode, int grid, cudaStream_t stream) {
+  if (mode == kPtrArray) {
+    transfer_rows_kernel<SlotT, VEC, kPtrArray><<<grid, kThreads, 0, stream>>>(p);
+  } else {
+    transfer_rows_kernel<SlotT, VEC, kDirect><<<grid, kThreads, 0, stream>>>(p);
+  }
+  return cudaGetLastError();
+}
+
+template <typename SlotT>
+cudaError_t launch_slot(const TransferParams& p, int vec, int mode, int grid,
+                        cudaStream_t stream) {
+  switch (vec) {
+    case 16: return launch_vec<SlotT, 16>(p, mode, grid, stream);
+    case 8: return launch_vec<SlotT, 8>(p, mode, grid, stream);
+    case 4: return launch_vec<SlotT, 4>(p, mode, grid, stream);
+    default: return launch_vec<SlotT, 2>(p, mode, grid, stream);
+  }
+}
+
+// Validates the common arguments, fills the derived fields of `p` and
+// launches. `alignment_terms` are the host-known addresses and strides that
+// must all be multiples of the vector width.
+int launch_transfer(TransferParams p, int type, int slot_type, int mode,
+                    std::initializer_list<uint64_t> alignment_terms,
+                    cudaStream_t stream, const char* who) {
+  const int esz = dtype_size(type);
+  if (esz == 0) {
+    return fail(LMCB_ERR_UNSUPPORTED_DTYPE, std::string(who) + ": ScalarType not supported.");
+  }
+  if (slot_type != LMCB_DTYPE_INT64 && slot_type != LMCB_DTYPE_INT32) {
+    return fail(LMCB_ERR_UNSUPPORTED_DTYPE,
+                std::string(who) + ": slot ids must be int64 or int32.");
+  }
+  if (p.num_tokens < 0 || p.num_layers < 0 || p.row_bytes <= 0) {
+    return fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": negative size.");
+  }
+  if (p.num_tokens == 0 || p.num_layers == 0) return LMCB_OK;
+  if (p.lmc == nullptr || p.slots == nullptr) {
+    return fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": NULL pointer.");
+  }
+  if (mode == kPtrArray && (p.ptrs_k == nullptr || p.ptrs_v == nullptr)) {
+    return fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": NULL pointer array.");
+  }
+  if (mode == kDirect && (p.base_k == nullptr || (p.num_kv > 1 && p.base_v == nullptr))) {
+    return fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": NULL cache pointer.");
+  }
+  p.status = device_status_ptr();
+  if (p.status == nullptr) return LMCB_ERR_CUDA;
+
+  int vec = pick_vec(alignment_terms);
+  if (vec < 2) vec = 2;  // every supported element is >= 2 bytes
+  const int64_t row_vecs = p.row_bytes / vec;
+  int64_t tile_rows = kTargetTileBytes / p.row_bytes;
+  if (tile_rows < 1) tile_rows = 1;
+  if (tile_rows > kMaxTileRows) tile_rows = kMaxTileRows;
+  // The flat item index (rows * row_vecs) must stay below 2^31.
+  while (tile_rows > 1 && tile_rows * row_vecs >= (int64_t(1) << 31)) tile_rows >>= 1;
+  if (row_vecs >= (int64_t(1) << 31)) {
+    return fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": row too long.");
+  }
+  p.tile_rows = static_cast<int32_t>(tile_rows);
+  p.tiles_per_seq = static_cast<int32_t>((p.num_tokens + tile_rows - 1) / tile_rows);
+  p.num_tiles = static_cast<int64_t>(p.num_kv) * p.num_layers * p.tiles_per_seq;
+  p.row_vecs = FastDiv(static_cast<uint32_t>(row_vecs));
+
+  const int64_t max_grid = static_cast<int64_t>(current_sm_count()) * 8;
+  const int grid = static_cast<int>(p.num_tiles < max_grid ? p.num_tiles : max_grid);
+
+  cudaError_t err = slot_type == LMCB_DTYPE_INT64
+                        ? launch_slot<int64_t>(p, vec, mode, grid, stream)
+                        : launch_slot<int32_t>(p, vec, mode, grid, stream);
+  if (err != cudaSuccess) return cuda_fail(err, who);
+  return LMCB_OK;
+}
+
+}  // namespace
+}  // namespace lmcb
+
+using lmcb::TransferParams;
+
+extern "C" {
+
+int lmcb_multi_layer_kv_transfer_kernel(int type, int slotType, void* stream,
+                                        const uint64_t* pagedKVCaches,
+                                        void* dstCacheTensor,
+                                        const void* slotmappings,
+                                        int64_t hiddenDims, int32_t kvs,
+                                        int32_t numLayers, int64_t pageBuffSize,
+                                        int32_t numTokensChunk, int page2L) {
+  lmcb::clear_error();
+  const char* who = "multi_layer_kv_transfer";
+  if (kvs != 1 && kvs != 2) {
+    return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": kvs must be 1 or 2.");
+  }
+  if (kvs == 2 && pageBuffSize <= 0) {
+    return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT,
+                      std::string(who) + ": page_buffer_size must be positive for K/V caches.");
+  }
+  const int64_t esz = lmcb::dtype_size(type);
+  const int64_t row = hiddenDims * esz;
+  TransferParams p{};
+  p.lmc = static_cast<uint8_t*>(dstCacheTensor);
+  p.lmc_token_stride = row;
+  p.lmc_layer_stride = row * numTokensChunk;
+  p.lmc_kv_stride = p.lmc_layer_stride * numLayers;
+  p.ptrs_k = pagedKVCaches;
+  p.ptrs_v = pagedKVCaches;
+  p.page_kv_offset = pageBuffSize * row;
+  p.paged_row_stride = row;
+  p.num_paged_rows = pageBuffSize;
+  p.slots = slotmappings;
+  p.num_tokens = numTokensChunk;
+  p.num_layers = numLayers;
+  p.num_kv = kvs;
+  p.row_bytes = row;
+  p.page2L = page2L ? 1 : 0;
+  if (esz == 0) p.row_bytes = 1;  // rejected in launch_transfer
+  return lmcb::launch_transfer(
+      p, type, slotType, lmcb::kPtrArray,
+      {reinterpret_cast<uint64_t>(dstCacheTensor), static_cast<uint64_t>(row),
+       static_cast<uint64_t>(p.page_kv_offset)},
+      static_cast<cudaStream_t>(stream), who);
+}
+
+int lmcb_multi_layer_kv_transfer_unilateral_kernel(
+    int type, int slotType, void* stream, const uint64_t* keyPtrs,
+    const uint64_t* valuePtrs, void* dstCacheTensor, const void* slotmappings,
+    int64_t hiddenDims, int32_t numLayers, int64_t pageBuffSize,
+    int32_t numTokensChunk, int page2L) {
+  lmcb::clear_error();
+  const char* who = "multi_layer_kv_transfer_unilateral";
+  const int64_t esz = lmcb::dtype_size(type);
+  const int64_t row = hiddenDims * esz;
+  TransferParams p{};
+  p.lmc = static_cast<uint8_t*>(dstCacheTensor);
+  p.lmc_token_stride = row;
+  p.lmc_layer_stride = row * numTokensChunk;
+  p.lmc_kv_stride = p.lmc_layer_stride * numLayers;
+  p.ptrs_k = keyPtrs;
+  p.ptrs_v = valuePtrs;
+  p.page_kv_offset = 0;
+  p.paged_row_stride = row;
+  p.num_paged_rows = pageBuffSize;
+  p.slots = slotmappings;
+  p.num_tokens = numTokensChunk;
+  p.num_layers = numLayers;
+  p.num_kv = 2;
+  p.row_bytes = esz == 0 ? 1 : row;
+  p.page2L = page2L ? 1 : 0;
+  return lmcb::launch_transfer(
+      p, type, slotType, lmcb::kPtrArray,
+      {reinterpret_cast<uint64_t>(dstCacheTensor), static_cast<uint64_t>(row)},
+      static_cast<cudaStream_t>(stream), who);
+}
+
+int lmcb_single_layer_kv_transfer_kernel(int type, int slotType, void* stream,
+                                         void* dstCacheTensor, void* keyCachePtr,
+                                         void* valueCachePtr,
+                                         const void* slotmappings,
+                                         int64_t hiddenDims, int32_t numTokens,
+                                         int page2L, int tokenMajor, int isMLA,
+                                         int64_t pagedRowStride,
+                                         int64_t numPagedRows) {
+  lmcb::clear_error();
+  const char* who = "single_layer_kv_transfer";
+  const int64_t esz = lmcb::dtype_size(type);
+  const int64_t row = hiddenDims * esz;
+  const int kvs = isMLA ? 1 : 2;
+  TransferParams p{};
+  p.lmc = static_cast<uint8_t*>(dstCacheTensor);
+  if (isMLA) {
+    p.lmc_token_stride = row;
+    p.lmc_kv_stride = 0;
+  } else if (tokenMajor) {
+    p.lmc_token_stride = 2 * row;  // [T, 2, H]
+    p.lmc_kv_stride = row;
+  } else {
+    p.lmc_token_stride = row;      // [2, T, H]
+    p.lmc_kv_stride = row * numTokens;
+  }
+  p.lmc_layer_stride = 0;
+  p.base_k = static_cast<uint8_t*>(keyCachePtr);
+  p.base_v = static_cast<uint8_t*>(valueCachePtr);
+  p.paged_row_stride = pagedRowStride > 0 ? pagedRowStride : row;
+  p.num_paged_rows = numPagedRows;
+  p.slots = slotmappings;
+  p.num_tokens = numTokens;
+  p.num_layers = 1;
+  p.num_kv = kvs;
+  p.row_bytes = esz == 0 ? 1 : row;
+  p.page2L = page2L ? 1 : 0;
+  return lmcb::launch_transfer(
+      p, type, slotType, lmcb::kDirect,
+      {reinterpret_cast<uint64_t>(dstCacheTensor), static_cast<uint64_t>(row),
+       reinterpret_cast<uint64_t>(keyCachePtr),
+       isMLA ? 0 : reinterpret_cast<uint64_t>(valueCachePtr),
+       static_cast<uint64_t>(p.paged_row_stride)},
+      static_cast<cudaStream_t>(stream), who);
+}
+
+int lmcb_load_and_reshape_flash_kernel(int type, int slotType, void* stream,
+                                       void* dstCacheTensor, void* keyCachePtr,
+                                       void* valueCachePtr,
+                                       const void* slotmappings,
+                                       int64_t hiddenDims, int64_t numPages,
+                                       int32_t pagedSize, int32_t numTokens,
+                                       int32_t numLayers, int32_t layerIdx,
+                                       int page2L, int64_t pagedRowStride) {
+  lmcb::clear_error();
+  const char* who = page2L ? "load_and_reshape_flash" : "reshape_and_cache_back_flash";
+  if (layerIdx < 0 || layerIdx >= numLayers) {
+    return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT,
+                      std::string(who) + ": layer_idx out of range.");
+  }
+  const int64_t esz = lmcb::dtype_size(type);
+  const int64_t row = hiddenDims * esz;
+  TransferParams p{};
+  // Layer `layerIdx` of a [2, numLayers, numTokens, H] object.
+  p.lmc = static_cast<uint8_t*>(dstCacheTensor) +
+          static_cast<int64_t>(layerIdx) * numTokens * row;
+  p.lmc_token_stride = row;
+  p.lmc_layer_stride = 0;
+  p.lmc_kv_stride = row * numTokens * numLayers;
+  p.base_k = static_cast<uint8_t*>(keyCachePtr);
+  p.base_v = static_cast<uint8_t*>(valueCachePtr);
+  p.paged_row_stride = pagedRowStride > 0 ? pagedRowStride : row;
+  p.num_paged_rows = numPages * static_cast<int64_t>(pagedSize);
+  p.slots = slotmappings;
+  p.num_tokens = numTokens;
+  p.num_layers = 1;
+  p.num_kv = 2;
+  p.row_bytes = esz == 0 ? 1 : row;
+  p.page2L = page2L ? 1 : 0;
+  return lmcb::launch_transfer(
+      p, type, slotType, lmcb::kDirect,
+      {reinterpret_cast<uint64_t>(p.lmc), static_cast<uint64_t>(row),
+       static_cast<uint64_t>(p.lmc_kv_stride),
+       reinterpret_cast<uint64_t>(keyCachePtr), reinterpret_cast<uint64_t>(valueCachePtr),
+       static_cast<uint64_t>(p.paged_row_stride)},
+      static_cast<cudaStream_t>(stream), who);
+}
+
+int lmcb_multi_layer_kv_retrieve_staged(int type, int slotType, void* stream,
+                                        const uint64_t* pagedKVCaches,
+                                        const void* hostCacheTensor,
+                                        void* staging, size_t stagingBytes,
+                                        const void* slotmappings,
+                                        int64_t hiddenDims, int32_t kvs,
+                                        int32_t numLayers, int64_t pageBuffSize,
+                                        int32_t numTokensChunk) {
+  lmcb::clear_error();
+  const int64_t esz = lmcb::dtype_size(type);
+  if (esz == 0) {
+    return lmcb::fail(LMCB_ERR_UNSUPPORTED_DTYPE,
+                      "multi_layer_kv_retrieve_staged: ScalarType not supported.");
+  }
+  if (numTokensChunk <= 0 || numLayers <= 0) return LMCB_OK;
+  const size_t bytes = static_cast<size_t>(kvs) * numLayers * numTokensChunk * hiddenDims * esz;
+  if (hostCacheTensor == nullptr || staging == nullptr) {
+    return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT, "multi_layer_kv_retrieve_staged: NULL pointer.");
+  }
+  if (stagingBytes < bytes) {
+    return lmcb::fail(LMCB_ERR_CAPACITY,
+                      "multi_layer_kv_retrieve_staged: staging buffer holds " +
+                          std::to_string(stagingBytes) + " bytes, the object needs " +
+                          std::to_string(bytes));
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  LMCB_CUDA_TRY(cudaMemcpyAsync(staging, hostCacheTensor, bytes, cudaMemcpyHostToDevice, s));
+  return lmcb_multi_layer_kv_transfer_kernel(type, slotType, stream, pagedKVCaches, staging,
+                                             slotmappings, hiddenDims, kvs, numLayers,
+                                             pageBuffSize, numTokensChunk, 0);
+}
+
+}  // extern "C"
