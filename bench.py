@@ -56,6 +56,8 @@ def parse_args():
     ap.add_argument("--cpu-max-blocks", type=int, default=1024,
                     help="paged blocks per layer of the host-resident CPU baseline buffers")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--skip-e2e", action="store_true",
+                    help="HBM leg only (kernel tuning runs; the line then has no e2e)")
     ap.add_argument("--blocks", type=int, default=None,
                     help="override paged blocks per layer (small profiling cases only)")
     return ap.parse_args()
@@ -271,6 +273,15 @@ def run_ours(args):
     clock_summary = clocks.summary()
 
     # ---- e2e: pinned-host objects through c_ops ------------------------
+    if args.skip_e2e:
+        if rank == 0:
+            print(json.dumps({"value": round(value, 2), "ms_per_step": round(t_ms / args.steps, 4),
+                              "achieved": round(achieved, 1),
+                              "frac": round(achieved / peaks["hbm_gbs"], 4),
+                              "store_avg_us": round(statistics.mean(store_ms) * 1e3, 2),
+                              "retrieve_avg_us": round(statistics.mean(retr_ms) * 1e3, 2),
+                              "clocks": clock_summary}), flush=True)
+        return
     obj_bytes = sum(torch.Size(spec.memobj_shape(len(c))).numel() * 2 for c in dev_chunks)
     arena = PinMemoryAllocator(obj_bytes + 256 * n_chunks + (1 << 20))
     host_objs = [arena.allocate(spec.memobj_shape(len(c)), torch.bfloat16).tensor

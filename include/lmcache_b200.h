@@ -70,6 +70,7 @@ typedef enum {
 #define LMCB_DEVICE_FLAG_SLOT_OUT_OF_RANGE 0x1u
 #define LMCB_DEVICE_FLAG_SYMBOL_OUT_OF_RANGE 0x2u
 #define LMCB_DEVICE_FLAG_STREAM_OVERFLOW 0x4u
+#define LMCB_DEVICE_FLAG_WAIT_TIMEOUT 0x8u
 
 /* Library version, "major.minor.patch". */
 LMCB_API const char* lmcb_version(void);

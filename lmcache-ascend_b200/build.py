@@ -15,6 +15,7 @@ from __future__ import annotations
 import argparse
 import concurrent.futures as cf
 import os
+import shutil
 import subprocess
 import sys
 import sysconfig
@@ -103,7 +104,10 @@ def build_extension(force: bool = False, verbose: bool = False) -> str:
     import torch as _t
     abi = int(bool(_t._C._GLIBCXX_USE_CXX11_ABI))
     cmd = [
-        os.environ.get("CXX", "g++"),
+        # The system g++ (not $CXX): the extension must link libstdc++
+        # dynamically, sharing torch's copy; a second, static copy breaks
+        # iostream/locale state across the boundary.
+        shutil.which("g++") or "g++",
         "-O2",
         "-std=c++17",
         "-fPIC",

@@ -25,6 +25,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstdlib>
+#include <cstring>
 #include <string>
 
 #include "common.cuh"
@@ -191,6 +193,284 @@ transfer_rows_kernel(const TransferParams p) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Bulk-copy (TMA) path for device-resident objects.
+//
+// Each CTA is one warp that owns a contiguous, balanced range of rows in
+// (kv, layer, token) order and streams it through a ring of shared-memory
+// stages with the asynchronous bulk-copy engine:
+//   load   cp.async.bulk global -> shared, completion counted in bytes on
+//          the stage's mbarrier;
+//   store  cp.async.bulk shared -> global (bulk_group), whose smem reads are
+//          awaited with cp.async.bulk.wait_group.read before the stage is
+//          refilled.
+// Lane i of a group handles row i of the group. Consecutive rows whose source
+// and destination are both contiguous (consecutive slots in the paged buffer
+// and consecutive tokens in the object, e.g. all tokens of one page) are
+// merged into one copy issued by the run's first lane. Loads are plain
+// (single-CTA) bulk copies; the kernel needs no cluster launch.
+// ---------------------------------------------------------------------------
+
+constexpr int kBulkMaxStages = 8;
+constexpr uint32_t kWaitSpinLimit = 1u << 22;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(smem_dst)),
+      "l"(__cvta_generic_to_global(gsrc)), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_store(void* gdst, const void* smem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(
+                   __cvta_generic_to_global(gdst)),
+               "r"(smem_addr(smem_src)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_read_all_but_one() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+struct BulkParams {
+  int64_t num_rows;      // num_kv * num_layers * num_tokens
+  int32_t stage_rows;    // rows per stage (<= 32)
+  int32_t stages;        // ring depth (<= kBulkMaxStages)
+  int32_t stage_bytes;   // bytes per stage (>= stage_rows * row_bytes)
+};
+
+template <typename SlotT, int MODE>
+__global__ void __launch_bounds__(32)
+transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* data = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(b.stages) * b.stage_bytes);
+  uint64_t* s_dst = bars + kBulkMaxStages;                                // [stages][32]
+  uint32_t* s_len = reinterpret_cast<uint32_t*>(s_dst + kBulkMaxStages * 32);  // [stages][32]
+
+  const int lane = threadIdx.x;
+  const SlotT* __restrict__ slots = static_cast<const SlotT*>(p.slots);
+  const int64_t r_begin = b.num_rows * blockIdx.x / gridDim.x;
+  const int64_t r_end = b.num_rows * (blockIdx.x + 1) / gridDim.x;
+  const int64_t n_groups = (r_end - r_begin + b.stage_rows - 1) / b.stage_rows;
+  const int64_t rows_per_kv = static_cast<int64_t>(p.num_layers) * p.num_tokens;
+  const uint32_t row_bytes = static_cast<uint32_t>(p.row_bytes);
+
+  if (lane == 0) {
+    for (int s = 0; s < b.stages; ++s) mbar_init(&bars[s], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
+
+  // Resolves the group's rows, merges contiguous runs and starts their loads
+  // into stage `st`.
+  auto issue_load = [&](int64_t g, int st) {
+    const int64_t r = r_begin + g * b.stage_rows + lane;
+    bool valid = lane < b.stage_rows && r < r_end;
+    const uint8_t* src = nullptr;
+    uint8_t* dst = nullptr;
+    if (valid) {
+      const int kv = static_cast<int>(r / rows_per_kv);
+      const int64_t rem = r - kv * rows_per_kv;
+      const int layer = static_cast<int>(rem / p.num_tokens);
+      const int t = static_cast<int>(rem - static_cast<int64_t>(layer) * p.num_tokens);
+      const int64_t slot = static_cast<int64_t>(slots[t]);
+      valid = slot >= 0;
+      if (valid && p.num_paged_rows > 0 && slot >= p.num_paged_rows) {
+        valid = false;
+        raise_flag(p.status, LMCB_DEVICE_FLAG_SLOT_OUT_OF_RANGE);
+      }
+      if (valid) {
+        uint8_t* paged;
+        if (MODE == kPtrArray) {
+          const uint64_t* arr = kv == 0 ? p.ptrs_k : p.ptrs_v;
+          paged = reinterpret_cast<uint8_t*>(arr[layer]) + kv * p.page_kv_offset;
+        } else {
+          paged = kv == 0 ? p.base_k : p.base_v;
+        }
+        paged += slot * p.paged_row_stride;
+        uint8_t* lmc = p.lmc + kv * p.lmc_kv_stride + layer * p.lmc_layer_stride +
+                       static_cast<int64_t>(t) * p.lmc_token_stride;
+        src = p.page2L ? paged : lmc;
+        dst = p.page2L ? lmc : paged;
+        if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) != 0) {
+          // Not 16-byte aligned (only possible through the pointer array):
+          // copy this row here, byte-wise, and leave it out of the bulk ring.
+          for (uint32_t i = 0; i < row_bytes; ++i) dst[i] = src[i];
+          valid = false;
+        }
+      }
+    }
+    const uint8_t* prev_src = reinterpret_cast<const uint8_t*>(
+        __shfl_up_sync(0xffffffffu, reinterpret_cast<uintptr_t>(src), 1));
+    uint8_t* prev_dst = reinterpret_cast<uint8_t*>(
+        __shfl_up_sync(0xffffffffu, reinterpret_cast<uintptr_t>(dst), 1));
+    const bool prev_valid = __shfl_up_sync(0xffffffffu, valid ? 1 : 0, 1) != 0;
+    const bool cont = valid && lane > 0 && prev_valid && src == prev_src + row_bytes &&
+                      dst == prev_dst + row_bytes;
+    const uint32_t cont_mask = __ballot_sync(0xffffffffu, cont);
+    const bool head = valid && !cont;
+    uint32_t run = 0;
+    if (head) {
+      // Rows lane, lane+1, ... while the following lanes continue the run.
+      const uint32_t after = lane == 31 ? 0u : (cont_mask >> (lane + 1));
+      run = 1 + static_cast<uint32_t>(__ffs(~after) - 1);
+    }
+    const uint32_t bytes = run * row_bytes;
+    const uint32_t total = __reduce_add_sync(0xffffffffu, bytes);
+    if (lane == 0) mbar_arrive_expect_tx(&bars[st], total);
+    __syncwarp();
+    uint8_t* stage_slot = data + static_cast<size_t>(st) * b.stage_bytes + lane * row_bytes;
+    if (bytes) bulk_load(stage_slot, src, bytes, &bars[st]);
+    s_dst[st * 32 + lane] = reinterpret_cast<uint64_t>(dst);
+    s_len[st * 32 + lane] = bytes;
+  };
+
+  int64_t issued = 0;
+  for (; issued < n_groups && issued < b.stages; ++issued) issue_load(issued, static_cast<int>(issued));
+
+  bool timed_out = false;
+  for (int64_t g = 0; g < n_groups; ++g) {
+    const int st = static_cast<int>(g % b.stages);
+    const uint32_t parity = static_cast<uint32_t>((g / b.stages) & 1);
+    uint32_t spins = 0;
+    while (!mbar_try_wait(&bars[st], parity)) {
+      if (++spins >= kWaitSpinLimit) {
+        timed_out = true;
+        break;
+      }
+    }
+    if (__any_sync(0xffffffffu, timed_out)) {
+      if (lane == 0) raise_flag(p.status, LMCB_DEVICE_FLAG_WAIT_TIMEOUT);
+      // Give the loads still in flight a bounded chance to land before the
+      // CTA (and its shared memory) goes away.
+      for (int64_t g2 = g + 1; g2 < issued; ++g2) {
+        const int st2 = static_cast<int>(g2 % b.stages);
+        const uint32_t par2 = static_cast<uint32_t>((g2 / b.stages) & 1);
+        for (uint32_t k = 0; k < kWaitSpinLimit && !mbar_try_wait(&bars[st2], par2); ++k) {
+        }
+      }
+      break;
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    const uint32_t len = s_len[st * 32 + lane];
+    if (len) {
+      bulk_store(reinterpret_cast<void*>(s_dst[st * 32 + lane]),
+                 data + static_cast<size_t>(st) * b.stage_bytes + lane * row_bytes, len);
+    }
+    bulk_commit();
+    if (g >= 1 && issued < n_groups) {
+      // The previous group's stage is free once its store has read it.
+      bulk_wait_read_all_but_one();
+      issue_load(issued, static_cast<int>(issued % b.stages));
+      ++issued;
+    }
+  }
+  bulk_wait_all();
+}
+
+struct BulkConfig {
+  int stages;
+  int stage_kb;
+  int ctas_per_sm;
+};
+
+int env_int(const char* name, int dflt) {
+  const char* v = std::getenv(name);
+  if (v == nullptr || *v == 0) return dflt;
+  return std::atoi(v);
+}
+
+// Ring geometry; LMCB_BULK_STAGES / LMCB_BULK_STAGE_KB / LMCB_BULK_CTAS_PER_SM
+// override the defaults (tuning only; read on every call so a process can
+// compare settings).
+BulkConfig bulk_config() {
+  BulkConfig c;
+  c.stages = env_int("LMCB_BULK_STAGES", 4);
+  c.stage_kb = env_int("LMCB_BULK_STAGE_KB", 16);
+  c.ctas_per_sm = env_int("LMCB_BULK_CTAS_PER_SM", 3);
+  if (c.stages < 2) c.stages = 2;
+  if (c.stages > kBulkMaxStages) c.stages = kBulkMaxStages;
+  if (c.stage_kb < 4) c.stage_kb = 4;
+  if (c.stage_kb > 64) c.stage_kb = 64;
+  while (c.stages * c.stage_kb > 192 && c.stages > 2) --c.stages;  // per-CTA smem cap
+  if (c.stages * c.stage_kb > 192) c.stage_kb = 96;
+  if (c.ctas_per_sm < 1) c.ctas_per_sm = 1;
+  if (c.ctas_per_sm > 16) c.ctas_per_sm = 16;
+  return c;
+}
+
+size_t bulk_smem_bytes(const BulkParams& b) {
+  return static_cast<size_t>(b.stages) * b.stage_bytes + kBulkMaxStages * sizeof(uint64_t) +
+         kBulkMaxStages * 32 * (sizeof(uint64_t) + sizeof(uint32_t));
+}
+
+template <typename SlotT>
+cudaError_t launch_bulk(const TransferParams& p, const BulkParams& b, int mode, int grid,
+                        cudaStream_t stream) {
+  const size_t smem = bulk_smem_bytes(b);
+  const void* fn = mode == kPtrArray
+                       ? reinterpret_cast<const void*>(&transfer_rows_bulk_kernel<SlotT, kPtrArray>)
+                       : reinterpret_cast<const void*>(&transfer_rows_bulk_kernel<SlotT, kDirect>);
+  cudaError_t err =
+      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (err != cudaSuccess) return err;
+  if (mode == kPtrArray) {
+    transfer_rows_bulk_kernel<SlotT, kPtrArray><<<grid, 32, smem, stream>>>(p, b);
+  } else {
+    transfer_rows_bulk_kernel<SlotT, kDirect><<<grid, 32, smem, stream>>>(p, b);
+  }
+  return cudaGetLastError();
+}
+
+// True when `ptr` is device memory of the current context (not a host
+// mapping); bulk copies are used only between device buffers.
+bool is_device_memory(const void* ptr) {
+  cudaPointerAttributes attr{};
+  if (cudaPointerGetAttributes(&attr, ptr) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return attr.type == cudaMemoryTypeDevice;
+}
+
 // Largest power of two <= 16 dividing every value in `vals`.
 int pick_vec(std::initializer_list<uint64_t> vals) {
   uint64_t g = 0;
@@ -255,6 +535,39 @@ int launch_transfer(TransferParams p, int type, int slot_type, int mode,
 
   int vec = pick_vec(alignment_terms);
   if (vec < 2) vec = 2;  // every supported element is >= 2 bytes
+
+  // Path choice: bulk copies when both sides are device memory, rows are
+  // 16-byte multiples and fit a stage; LMCB_TRANSFER_PATH=vector|bulk forces
+  // one (bulk still requires those conditions).
+  const int forced = [] {
+    const char* v = std::getenv("LMCB_TRANSFER_PATH");
+    if (v == nullptr) return 0;
+    if (std::strcmp(v, "vector") == 0) return 1;
+    if (std::strcmp(v, "bulk") == 0) return 2;
+    return 0;
+  }();
+  const BulkConfig bc = bulk_config();
+  const int64_t stage_bytes = static_cast<int64_t>(bc.stage_kb) * 1024;
+  const bool bulk_ok = vec == 16 && p.row_bytes % 16 == 0 && p.row_bytes <= stage_bytes &&
+                       is_device_memory(p.lmc);
+  if (bulk_ok && forced != 1) {
+    BulkParams b;
+    b.num_rows = static_cast<int64_t>(p.num_kv) * p.num_layers * p.num_tokens;
+    int64_t rows = stage_bytes / p.row_bytes;
+    b.stage_rows = static_cast<int32_t>(rows > 32 ? 32 : rows);
+    b.stages = bc.stages;
+    b.stage_bytes = static_cast<int32_t>(stage_bytes);
+    int64_t grid = static_cast<int64_t>(current_sm_count()) * bc.ctas_per_sm;
+    const int64_t groups = (b.num_rows + b.stage_rows - 1) / b.stage_rows;
+    if (grid > groups) grid = groups;
+    if (grid < 1) grid = 1;
+    cudaError_t err = slot_type == LMCB_DTYPE_INT64
+                          ? launch_bulk<int64_t>(p, b, mode, static_cast<int>(grid), stream)
+                          : launch_bulk<int32_t>(p, b, mode, static_cast<int>(grid), stream);
+    if (err != cudaSuccess) return cuda_fail(err, who);
+    return LMCB_OK;
+  }
+
   const int64_t row_vecs = p.row_bytes / vec;
   int64_t tile_rows = kTargetTileBytes / p.row_bytes;
   if (tile_rows < 1) tile_rows = 1;

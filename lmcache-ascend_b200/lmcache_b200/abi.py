@@ -34,6 +34,7 @@ LMCB_DTYPE_INT32 = 4
 LMCB_DEVICE_FLAG_SLOT_OUT_OF_RANGE = 0x1
 LMCB_DEVICE_FLAG_SYMBOL_OUT_OF_RANGE = 0x2
 LMCB_DEVICE_FLAG_STREAM_OVERFLOW = 0x4
+LMCB_DEVICE_FLAG_WAIT_TIMEOUT = 0x8
 
 # name -> (restype, argtypes)
 SIGNATURES: dict[str, tuple] = {

@@ -9,6 +9,7 @@ from __future__ import annotations
 import ctypes
 import glob
 import os
+import shutil
 import subprocess
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -29,7 +30,7 @@ def build(force: bool = False) -> str | None:
         t = os.path.getmtime(LIB)
         if all(os.path.getmtime(s) <= t for s in srcs + glob.glob(os.path.join(HERE, "*.h"))):
             return LIB
-    cmd = [os.environ.get("CC", "gcc"), "-O2", "-std=c11", "-fPIC", "-shared", "-Wall",
+    cmd = [shutil.which("gcc") or "gcc", "-O2", "-std=c11", "-fPIC", "-shared", "-Wall",
            "-Werror", *srcs, "-o", LIB]
     subprocess.run(cmd, check=True)
     return LIB

@@ -53,6 +53,21 @@ def ptrs_of(caches):
     return torch.tensor([c.data_ptr() for c in caches], dtype=torch.int64).to(DEV)
 
 
+@pytest.fixture(params=["auto", "vector", "bulk-small-ring"])
+def transfer_path(request, monkeypatch):
+    """Runs a test under the default path choice, the vectorised LD/ST kernel,
+    and the bulk-copy kernel with a minimal ring (2 stages of 4 KB) so stage
+    reuse and partial groups are exercised."""
+    if request.param == "vector":
+        monkeypatch.setenv("LMCB_TRANSFER_PATH", "vector")
+    elif request.param == "bulk-small-ring":
+        monkeypatch.setenv("LMCB_TRANSFER_PATH", "bulk")
+        monkeypatch.setenv("LMCB_BULK_STAGES", "2")
+        monkeypatch.setenv("LMCB_BULK_STAGE_KB", "4")
+        monkeypatch.setenv("LMCB_BULK_CTAS_PER_SM", "1")
+    return request.param
+
+
 @pytest.fixture(scope="module")
 def pin_alloc():
     a = PinMemoryAllocator(3 << 30)
@@ -67,7 +82,7 @@ def pin_alloc():
 
 @pytest.mark.parametrize("num_tokens", [256, 500, 1024, 8000])
 @pytest.mark.parametrize("memobj_on", ["hbm", "pinned"])
-def test_multi_layer_kernel(num_tokens, memobj_on, pin_alloc):
+def test_multi_layer_kernel(num_tokens, memobj_on, pin_alloc, transfer_path):
     num_layers, num_blocks, block_size, heads, hd, chunk = 32, 1000, 16, 8, 128, 256
     dtype = torch.bfloat16
     pbs = num_blocks * block_size
@@ -114,7 +129,7 @@ def test_multi_layer_kernel(num_tokens, memobj_on, pin_alloc):
 
 
 @pytest.mark.parametrize("num_tokens", [256, 500, 1024, 8000])
-def test_multi_layer_kernel_use_mla(num_tokens, pin_alloc):
+def test_multi_layer_kernel_use_mla(num_tokens, pin_alloc, transfer_path):
     num_layers, num_blocks, block_size, hd, chunk = 32, 1000, 64, 576, 256
     dtype = torch.bfloat16
     kv = kv_list(num_layers, num_blocks, block_size, 1, hd, dtype, seed=7 + num_tokens, mla=True)
@@ -123,8 +138,12 @@ def test_multi_layer_kernel_use_mla(num_tokens, pin_alloc):
     ptrs = ptrs_of(kv)
     kv_np = [bits(t) for t in kv]
     objs = []
-    for sc in torch.split(slots_dev, chunk):
-        obj = pin_alloc.allocate([1, num_layers, len(sc), hd], dtype)
+    for i, sc in enumerate(torch.split(slots_dev, chunk)):
+        if i % 2:
+            obj = pin_alloc.allocate([1, num_layers, len(sc), hd], dtype)
+        else:  # alternate pinned-host and HBM objects
+            obj = type("Obj", (), {})()
+            obj.tensor = torch.empty([1, num_layers, len(sc), hd], dtype=dtype, device=DEV)
         obj.tensor.zero_()
         # page_buffer_size = 0 as the reference's MLA callers pass it (:359).
         c_ops.multi_layer_kv_transfer(obj.tensor, ptrs, sc, kv[0].device, 0, True, True)
@@ -142,8 +161,9 @@ def test_multi_layer_kernel_use_mla(num_tokens, pin_alloc):
     for a, b in zip(kv, kv_new):
         fa, fb = a.reshape(-1, hd), b.reshape(-1, hd)
         assert torch.equal(fa[slots_dev], fb[slots_dev])
-    for obj in objs:
-        pin_alloc.free(obj)
+    for i, obj in enumerate(objs):
+        if i % 2:
+            pin_alloc.free(obj)
 
 
 # ---------------------------------------------------------------------------
@@ -153,7 +173,7 @@ def test_multi_layer_kernel_use_mla(num_tokens, pin_alloc):
 
 @pytest.mark.parametrize("num_tokens", [256, 500, 1024, 8000])
 @pytest.mark.parametrize("token_major", [True, False])
-def test_single_layer_kernel(num_tokens, token_major):
+def test_single_layer_kernel(num_tokens, token_major, transfer_path):
     num_layers, num_blocks, block_size, heads, hd = 32, 1000, 16, 8, 128
     dtype = torch.bfloat16
     H = heads * hd
@@ -191,7 +211,7 @@ def test_single_layer_kernel(num_tokens, token_major):
 
 
 @pytest.mark.parametrize("num_tokens", [256, 500, 1024, 8000])
-def test_extract_and_load_back(num_tokens, pin_alloc):
+def test_extract_and_load_back(num_tokens, pin_alloc, transfer_path):
     num_layers, num_blocks, block_size, heads, hd, chunk = 32, 1000, 16, 8, 128, 256
     dtype = torch.bfloat16
     H = heads * hd
@@ -202,8 +222,12 @@ def test_extract_and_load_back(num_tokens, pin_alloc):
     slots = seeded_slots(num_blocks * block_size, num_tokens, seed=num_tokens + 2, n_neg=3)
     slots_dev = slots.to(DEV)
     objs = []
-    for sc in torch.split(slots_dev, chunk):
-        obj = pin_alloc.allocate([2, num_layers, len(sc), H], dtype)
+    for i, sc in enumerate(torch.split(slots_dev, chunk)):
+        if i % 2:
+            obj = pin_alloc.allocate([2, num_layers, len(sc), H], dtype)
+        else:  # alternate pinned-host and HBM objects
+            obj = type("Obj", (), {})()
+            obj.tensor = torch.empty([2, num_layers, len(sc), H], dtype=dtype, device=DEV)
         obj.tensor.zero_()
         for layer in range(num_layers):
             c_ops.load_and_reshape_flash(obj.tensor, kv[layer][0], kv[layer][1], sc, layer)
@@ -227,8 +251,9 @@ def test_extract_and_load_back(num_tokens, pin_alloc):
             oracle.reshape_and_cache_back_flash(bits(obj.tensor), kw, vw, sc.numpy(), layer)
         assert np.array_equal(bits(kv_new[layer][0]), kw)
         assert np.array_equal(bits(kv_new[layer][1]), vw)
-    for obj in objs:
-        pin_alloc.free(obj)
+    for i, obj in enumerate(objs):
+        if i % 2:
+            pin_alloc.free(obj)
 
 
 # ---------------------------------------------------------------------------
@@ -239,7 +264,7 @@ def test_extract_and_load_back(num_tokens, pin_alloc):
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("slot_dtype", [torch.int64, torch.int32])
 @pytest.mark.parametrize("heads,hd", [(8, 128), (1, 128), (2, 48), (1, 3)])
-def test_dtypes_and_row_widths(dtype, slot_dtype, heads, hd):
+def test_dtypes_and_row_widths(dtype, slot_dtype, heads, hd, transfer_path):
     num_layers, num_blocks, block_size = 3, 40, 16
     pbs = num_blocks * block_size
     kv = kv_list(num_layers, num_blocks, block_size, heads, hd, dtype, seed=5)
@@ -259,7 +284,7 @@ def test_dtypes_and_row_widths(dtype, slot_dtype, heads, hd):
         assert np.array_equal(bits(a), b)
 
 
-def test_unilateral():
+def test_unilateral(transfer_path):
     num_layers, rows, heads, hd = 4, 512, 8, 128
     dtype = torch.bfloat16
     g = torch.Generator(device=DEV).manual_seed(2)
@@ -298,7 +323,7 @@ def test_empty_and_all_skipped():
     assert c_ops.device_status(torch.cuda.current_device()) == 0
 
 
-def test_out_of_range_slot_is_skipped_and_flagged():
+def test_out_of_range_slot_is_skipped_and_flagged(transfer_path):
     kv = kv_list(2, 8, 16, 8, 128, torch.bfloat16, seed=1)
     pbs = 8 * 16
     slots = torch.tensor([0, 5, pbs, pbs + 100, 127], dtype=torch.int64)
@@ -312,7 +337,7 @@ def test_out_of_range_slot_is_skipped_and_flagged():
     assert np.array_equal(bits(obj), want)
 
 
-def test_misaligned_layer_pointer_falls_back():
+def test_misaligned_layer_pointer_falls_back(transfer_path):
     """A layer base that is 2-byte but not 16-byte aligned is copied byte-wise."""
     heads, hd, nb, bs = 2, 64, 16, 16
     backing = torch.randn(2 * nb * bs * heads * hd + 1, device=DEV).to(torch.bfloat16)
