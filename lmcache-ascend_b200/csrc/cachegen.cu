@@ -351,11 +351,8 @@ int check_codec_args(const char* who, int L, int T, int C, int max_bins) {
   return LMCB_OK;
 }
 
-cudaError_t set_coder_smem(const void* kernel, size_t bytes) {
-  if (bytes <= 48 * 1024) return cudaSuccess;
-  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(bytes));
-}
+// Largest coder shared-memory footprint (max_bins = 256).
+inline size_t coder_smem_cap() { return coder_smem_bytes(kMaxBins); }
 
 }  // namespace
 }  // namespace lmcb
@@ -398,7 +395,7 @@ int lmcb_encode(const int16_t* cdf, const int8_t* inputSym, uint8_t* outputBuffe
   unsigned int* status = lmcb::device_status_ptr();
   if (status == nullptr) return LMCB_ERR_CUDA;
   const size_t smem = lmcb::coder_smem_bytes(maxBins);
-  LMCB_CUDA_TRY(lmcb::set_coder_smem(reinterpret_cast<const void*>(&lmcb::encode_kernel), smem));
+  LMCB_CUDA_TRY(lmcb::ensure_smem_limit<&lmcb::encode_kernel>(smem, lmcb::coder_smem_cap()));
   dim3 grid((numChannels + lmcb::kCoderThreads - 1) / lmcb::kCoderThreads, numLayers);
   lmcb::encode_kernel<<<grid, lmcb::kCoderThreads, smem, static_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const uint16_t*>(cdf), reinterpret_cast<const uint8_t*>(inputSym),
@@ -421,7 +418,7 @@ int lmcb_decode(const int16_t* cdf, const uint8_t* bytestreams, const int32_t* l
     return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT, "decode: NULL pointer.");
   }
   const size_t smem = lmcb::coder_smem_bytes(maxBins);
-  LMCB_CUDA_TRY(lmcb::set_coder_smem(reinterpret_cast<const void*>(&lmcb::decode_kernel), smem));
+  LMCB_CUDA_TRY(lmcb::ensure_smem_limit<&lmcb::decode_kernel>(smem, lmcb::coder_smem_cap()));
   dim3 grid((numChannels + lmcb::kCoderThreads - 1) / lmcb::kCoderThreads, numLayers);
   lmcb::decode_kernel<<<grid, lmcb::kCoderThreads, smem, static_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const uint16_t*>(cdf), bytestreams, lengths, nullptr,
@@ -442,7 +439,7 @@ int lmcb_decode_prefsum(const int16_t* cdf, const uint8_t* bytestreams, int64_t 
     return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT, "decode_prefsum: NULL pointer or negative size.");
   }
   const size_t smem = lmcb::coder_smem_bytes(maxBins);
-  LMCB_CUDA_TRY(lmcb::set_coder_smem(reinterpret_cast<const void*>(&lmcb::decode_kernel), smem));
+  LMCB_CUDA_TRY(lmcb::ensure_smem_limit<&lmcb::decode_kernel>(smem, lmcb::coder_smem_cap()));
   dim3 grid((numChannels + lmcb::kCoderThreads - 1) / lmcb::kCoderThreads, numLayers);
   lmcb::decode_kernel<<<grid, lmcb::kCoderThreads, smem, static_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const uint16_t*>(cdf), bytestreams, nullptr, endOffsets,

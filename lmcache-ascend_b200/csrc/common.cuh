@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <string>
 
 #include "lmcache_b200.h"
@@ -42,6 +43,30 @@ unsigned int* device_status_ptr();
 
 __device__ __forceinline__ void raise_flag(unsigned int* status, unsigned int flag) {
   atomicOr(status, flag);
+}
+
+// Raises kernel `Fn`'s dynamic shared-memory limit to max(bytes, cap) once
+// per device (the attribute call costs microseconds; later launches only
+// compare against the cached limit). One cache per kernel: Fn is a template
+// argument, not a parameter, so kernels with equal signatures stay distinct.
+template <auto Fn>
+cudaError_t ensure_smem_limit(size_t bytes, size_t cap) {
+  constexpr int kMaxDevices = 64;
+  static std::atomic<int> limit[kMaxDevices];
+  if (bytes <= 48 * 1024) return cudaSuccess;
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  const int want = static_cast<int>(bytes > cap ? bytes : cap);
+  if (dev < 0 || dev >= kMaxDevices) {
+    return cudaFuncSetAttribute(reinterpret_cast<const void*>(Fn),
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, want);
+  }
+  if (limit[dev].load(std::memory_order_relaxed) >= static_cast<int>(bytes)) return cudaSuccess;
+  err = cudaFuncSetAttribute(reinterpret_cast<const void*>(Fn),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, want);
+  if (err == cudaSuccess) limit[dev].store(want, std::memory_order_relaxed);
+  return err;
 }
 
 // Unsigned division by a loop-invariant divisor with a multiply-high and a

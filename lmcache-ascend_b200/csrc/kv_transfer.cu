@@ -25,6 +25,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 #include <string>
@@ -212,6 +213,9 @@ transfer_rows_kernel(const TransferParams p) {
 // ---------------------------------------------------------------------------
 
 constexpr int kBulkMaxStages = 8;
+// Upper bound of the ring's dynamic shared memory (stages * stage bytes plus
+// bookkeeping); the kernels' limit is raised to this once per device.
+constexpr size_t kBulkSmemCap = 200 * 1024;
 constexpr uint32_t kWaitSpinLimit = 1u << 22;
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
@@ -431,7 +435,6 @@ BulkConfig bulk_config() {
   if (c.stage_kb < 4) c.stage_kb = 4;
   if (c.stage_kb > 64) c.stage_kb = 64;
   while (c.stages * c.stage_kb > 192 && c.stages > 2) --c.stages;  // per-CTA smem cap
-  if (c.stages * c.stage_kb > 192) c.stage_kb = 96;
   if (c.ctas_per_sm < 1) c.ctas_per_sm = 1;
   if (c.ctas_per_sm > 16) c.ctas_per_sm = 16;
   return c;
@@ -446,23 +449,24 @@ template <typename SlotT>
 cudaError_t launch_bulk(const TransferParams& p, const BulkParams& b, int mode, int grid,
                         cudaStream_t stream) {
   const size_t smem = bulk_smem_bytes(b);
-  const void* fn = mode == kPtrArray
-                       ? reinterpret_cast<const void*>(&transfer_rows_bulk_kernel<SlotT, kPtrArray>)
-                       : reinterpret_cast<const void*>(&transfer_rows_bulk_kernel<SlotT, kDirect>);
-  cudaError_t err =
-      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  if (err != cudaSuccess) return err;
+  cudaError_t err;
   if (mode == kPtrArray) {
+    err = ensure_smem_limit<&transfer_rows_bulk_kernel<SlotT, kPtrArray>>(smem, kBulkSmemCap);
+    if (err != cudaSuccess) return err;
     transfer_rows_bulk_kernel<SlotT, kPtrArray><<<grid, 32, smem, stream>>>(p, b);
   } else {
+    err = ensure_smem_limit<&transfer_rows_bulk_kernel<SlotT, kDirect>>(smem, kBulkSmemCap);
+    if (err != cudaSuccess) return err;
     transfer_rows_bulk_kernel<SlotT, kDirect><<<grid, 32, smem, stream>>>(p, b);
   }
   return cudaGetLastError();
 }
 
-// True when `ptr` is device memory of the current context (not a host
-// mapping); bulk copies are used only between device buffers.
+// True when `ptr` is device memory (not a host mapping); bulk copies are
+// used only between device buffers. Registered host ranges are recognised
+// without a driver call.
 bool is_device_memory(const void* ptr) {
+  if (lmcb_host_get_device_ptr(const_cast<void*>(ptr)) != nullptr) return false;
   cudaPointerAttributes attr{};
   if (cudaPointerGetAttributes(&attr, ptr) != cudaSuccess) {
     cudaGetLastError();

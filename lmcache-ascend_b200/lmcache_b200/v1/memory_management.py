@@ -8,7 +8,7 @@ out of it (zero-copy over PCIe). Objects are dense views into the arena.
 
 The sub-allocator is first-fit over an address-ordered free list with
 coalescing on free, with 256-byte aligned blocks (so every object start is
-16-byte aligned for the vectorised kernels).
+16-byte aligned for the vectorised and bulk-copy kernels).
 """
 
 from __future__ import annotations
@@ -33,13 +33,19 @@ class MemoryObj:
     nbytes: int
 
 
-class PinMemoryAllocator:
-    """First-fit allocator over one pinned, host-registered buffer."""
+class TensorMemoryAllocator:
+    """First-fit allocator over one uint8 buffer (any device).
 
-    def __init__(self, size: int):
-        self.size = int(size)
-        self.buffer = torch.empty(self.size, dtype=torch.uint8, device="cpu", pin_memory=True)
-        c_ops.host_register(self.buffer)
+    Same contract as upstream LMCache's TensorMemoryAllocator as the
+    reference's tests use it (tests/v1/test_memory_management.py:22-67):
+    ``allocate`` returns None when nothing fits, ``free`` tolerates a second
+    free of the same object, ``memcheck`` validates the free list.
+    """
+
+    def __init__(self, buffer: torch.Tensor):
+        assert buffer.dtype == torch.uint8 and buffer.dim() == 1
+        self.buffer = buffer
+        self.size = buffer.numel()
         self._free: List[Tuple[int, int]] = [(0, self.size)]  # (offset, length), sorted
         self._lock = threading.Lock()
 
@@ -75,19 +81,30 @@ class PinMemoryAllocator:
         obj.tensor = None
 
     def memcheck(self) -> bool:
-        """Free blocks are in range, ordered, non-overlapping and coalesced."""
+        """Free blocks are in range, sorted, disjoint and coalesced."""
         with self._lock:
             prev_end = -1
             for off, length in self._free:
                 if off < 0 or length <= 0 or off + length > self.size or off <= prev_end:
                     return False
-                if off == prev_end:
-                    return False
                 prev_end = off + length
         return True
 
     def close(self) -> None:
+        pass
+
+
+class PinMemoryAllocator(TensorMemoryAllocator):
+    """A TensorMemoryAllocator over a pinned host buffer registered with
+    ``c_ops.host_register`` (lmcache_ascend/v1/memory_management.py:33-68)."""
+
+    def __init__(self, size: int):
+        buffer = torch.empty(int(size), dtype=torch.uint8, device="cpu", pin_memory=True)
+        c_ops.host_register(buffer)
+        super().__init__(buffer)
+
+    def close(self) -> None:
         try:
             c_ops.host_unregister(self.buffer)
-        except Exception:
+        except RuntimeError:
             pass
