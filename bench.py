@@ -175,6 +175,26 @@ def measured_peaks() -> dict:
         return {"hbm_gbs": 6650.0, "source": "fallback"}
 
 
+def measure_pcie(dev, stream, nbytes: int = 256 << 20, reps: int = 5) -> dict:
+    """Copy-engine bandwidth between pinned host and HBM (cudaMemcpyAsync of
+    `nbytes`, best of `reps`): the practical PCIe ceiling the pinned-host
+    legs are compared with."""
+    host = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    devbuf = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    out = {}
+    for name, (dst, src) in (("h2d", (devbuf, host)), ("d2h", (host, devbuf))):
+        best = 0.0
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            dst.copy_(src, non_blocking=True)
+            b.record(stream)
+            torch.cuda.synchronize()
+            best = max(best, nbytes / (a.elapsed_time(b) / 1e3) / 1e9)
+        out[name] = round(best, 2)
+    return out
+
+
 def committed_traffic(kernel: str, workload: str):
     """dram read+write bytes per launch from the committed ncu summary, if any."""
     path = os.path.join(ROOT, "profiles", f"{kernel}_{workload}.md")
@@ -360,6 +380,7 @@ def run_ours(args):
         dir_rates[label] = round(2 * payload / (s0.elapsed_time(s1) / 1e3) / 1e9, 2)
     os.environ.pop("LMCB_HOST_RETRIEVE", None)
     best_mode = max(e2e, key=e2e.get)
+    pcie = measure_pcie(dev, stream)
 
     # ---- CPU baseline (rank 0, N = 1) -----------------------------------
     cpu = None
@@ -421,6 +442,8 @@ def run_ours(args):
                 "path": f"pinned-host MemoryObj via c_ops; store zero-copy, retrieve {best_mode}",
                 "by_retrieve_path": {k: round(v, 2) for k, v in e2e.items()},
                 "per_direction_gbs": dir_rates,
+                "pcie_copy_engine_gbs": pcie,
+                "frac_of_copy_engine": round(e2e[best_mode] / ((pcie["h2d"] + pcie["d2h"]) / 2), 4),
             },
             "roofline": {
                 "bound": "hbm",

@@ -83,6 +83,15 @@ template <> struct VecType<8> { using T = uint2; };
 template <> struct VecType<4> { using T = uint32_t; };
 template <> struct VecType<2> { using T = uint16_t; };
 
+// Programmatic dependent launch: wait for the preceding kernel in the stream
+// (and the visibility of its writes) before touching global memory, and let
+// the next kernel be scheduled while this one runs. Both are no-ops when the
+// launch carries no programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 template <typename SlotT, int VEC, int MODE>
 __global__ void __launch_bounds__(kThreads)
 transfer_rows_kernel(const TransferParams p) {
@@ -95,6 +104,8 @@ transfer_rows_kernel(const TransferParams p) {
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
+  pdl_wait();
+  pdl_launch_dependents();
 
   for (int64_t tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
     // tile -> (kv, layer, token range); token tiles vary fastest so
@@ -273,11 +284,15 @@ __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
+constexpr int kBatchRows = 256;   // rows resolved together (8 per lane)
+
 struct BulkParams {
-  int64_t num_rows;      // num_kv * num_layers * num_tokens
+  int32_t num_rows;      // num_kv * num_layers * num_tokens (< 2^31)
   int32_t stage_rows;    // rows per stage (<= 32)
   int32_t stages;        // ring depth (<= kBulkMaxStages)
   int32_t stage_bytes;   // bytes per stage (>= stage_rows * row_bytes)
+  FastDiv div_tokens;    // row -> (kv * num_layers + layer, token)
+  FastDiv div_layers;    // (kv * num_layers + layer) -> (kv, layer)
 };
 
 template <typename SlotT, int MODE>
@@ -286,68 +301,120 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* data = smem;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(b.stages) * b.stage_bytes);
-  uint64_t* s_dst = bars + kBulkMaxStages;                                // [stages][32]
-  uint32_t* s_len = reinterpret_cast<uint32_t*>(s_dst + kBulkMaxStages * 32);  // [stages][32]
+  uint64_t* s_dst = bars + kBulkMaxStages;              // [kBulkMaxStages][32] store targets
+  uint64_t* tab_src = s_dst + kBulkMaxStages * 32;      // [kBatchRows] resolved sources
+  uint64_t* tab_dst = tab_src + kBatchRows;             // [kBatchRows] resolved destinations
+  uint32_t* s_len = reinterpret_cast<uint32_t*>(tab_dst + kBatchRows);  // [kBulkMaxStages][32]
 
   const int lane = threadIdx.x;
   const SlotT* __restrict__ slots = static_cast<const SlotT*>(p.slots);
-  const int64_t r_begin = b.num_rows * blockIdx.x / gridDim.x;
-  const int64_t r_end = b.num_rows * (blockIdx.x + 1) / gridDim.x;
-  const int64_t n_groups = (r_end - r_begin + b.stage_rows - 1) / b.stage_rows;
-  const int64_t rows_per_kv = static_cast<int64_t>(p.num_layers) * p.num_tokens;
+  const int32_t r_begin = static_cast<int32_t>(static_cast<int64_t>(b.num_rows) * blockIdx.x / gridDim.x);
+  const int32_t r_end = static_cast<int32_t>(static_cast<int64_t>(b.num_rows) * (blockIdx.x + 1) / gridDim.x);
+  const int32_t n_rows = r_end - r_begin;
   const uint32_t row_bytes = static_cast<uint32_t>(p.row_bytes);
+  // Groups never straddle a batch: a full batch holds ceil(kBatchRows /
+  // stage_rows) groups, the last partial batch the rest.
+  const int32_t groups_per_batch = (kBatchRows + b.stage_rows - 1) / b.stage_rows;
+  const int32_t full_batches = n_rows / kBatchRows;
+  const int32_t tail_rows = n_rows - full_batches * kBatchRows;
+  const int64_t n_groups = static_cast<int64_t>(full_batches) * groups_per_batch +
+                           (tail_rows + b.stage_rows - 1) / b.stage_rows;
 
   if (lane == 0) {
     for (int s = 0; s < b.stages; ++s) mbar_init(&bars[s], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncwarp();
+  pdl_wait();
+  pdl_launch_dependents();
 
-  // Resolves the group's rows, merges contiguous runs and starts their loads
-  // into stage `st`.
-  auto issue_load = [&](int64_t g, int st) {
-    const int64_t r = r_begin + g * b.stage_rows + lane;
-    bool valid = lane < b.stage_rows && r < r_end;
-    const uint8_t* src = nullptr;
-    uint8_t* dst = nullptr;
-    if (valid) {
-      const int kv = static_cast<int>(r / rows_per_kv);
-      const int64_t rem = r - kv * rows_per_kv;
-      const int layer = static_cast<int>(rem / p.num_tokens);
-      const int t = static_cast<int>(rem - static_cast<int64_t>(layer) * p.num_tokens);
-      const int64_t slot = static_cast<int64_t>(slots[t]);
-      valid = slot >= 0;
-      if (valid && p.num_paged_rows > 0 && slot >= p.num_paged_rows) {
+  // Resolves rows [b0, b0 + n) of this CTA's range into tab_src / tab_dst
+  // (0 for skipped rows). All slot ids and layer bases of the batch are
+  // loaded before any is used, so the batch costs one memory latency.
+  auto resolve_batch = [&](int32_t b0, int32_t n) {
+    constexpr int kPer = kBatchRows / 32;
+    int64_t slot[kPer];
+    uint8_t* base[kPer];
+    int kvs[kPer], layers[kPer], toks[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int idx = lane + 32 * j;
+      slot[j] = -1;
+      base[j] = nullptr;
+      kvs[j] = layers[j] = toks[j] = 0;
+      if (idx < n) {
+        const uint32_t r = static_cast<uint32_t>(r_begin + b0 + idx);
+        const uint32_t q = b.div_tokens.div(r);
+        toks[j] = static_cast<int>(r - q * b.div_tokens.d);
+        kvs[j] = static_cast<int>(b.div_layers.div(q));
+        layers[j] = static_cast<int>(q - kvs[j] * b.div_layers.d);
+        slot[j] = static_cast<int64_t>(slots[toks[j]]);
+        if (MODE == kPtrArray) {
+          const uint64_t* arr = kvs[j] == 0 ? p.ptrs_k : p.ptrs_v;
+          base[j] = reinterpret_cast<uint8_t*>(arr[layers[j]]) + kvs[j] * p.page_kv_offset;
+        } else {
+          base[j] = kvs[j] == 0 ? p.base_k : p.base_v;
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int idx = lane + 32 * j;
+      if (idx >= n) continue;
+      uint64_t src = 0, dst = 0;
+      bool valid = slot[j] >= 0;
+      if (valid && p.num_paged_rows > 0 && slot[j] >= p.num_paged_rows) {
         valid = false;
         raise_flag(p.status, LMCB_DEVICE_FLAG_SLOT_OUT_OF_RANGE);
       }
       if (valid) {
-        uint8_t* paged;
-        if (MODE == kPtrArray) {
-          const uint64_t* arr = kv == 0 ? p.ptrs_k : p.ptrs_v;
-          paged = reinterpret_cast<uint8_t*>(arr[layer]) + kv * p.page_kv_offset;
-        } else {
-          paged = kv == 0 ? p.base_k : p.base_v;
-        }
-        paged += slot * p.paged_row_stride;
-        uint8_t* lmc = p.lmc + kv * p.lmc_kv_stride + layer * p.lmc_layer_stride +
-                       static_cast<int64_t>(t) * p.lmc_token_stride;
-        src = p.page2L ? paged : lmc;
-        dst = p.page2L ? lmc : paged;
-        if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) != 0) {
+        uint8_t* paged = base[j] + slot[j] * p.paged_row_stride;
+        uint8_t* lmc = p.lmc + kvs[j] * p.lmc_kv_stride + layers[j] * p.lmc_layer_stride +
+                       static_cast<int64_t>(toks[j]) * p.lmc_token_stride;
+        uint8_t* s = p.page2L ? paged : lmc;
+        uint8_t* d = p.page2L ? lmc : paged;
+        if (((reinterpret_cast<uintptr_t>(s) | reinterpret_cast<uintptr_t>(d)) & 15) != 0) {
           // Not 16-byte aligned (only possible through the pointer array):
           // copy this row here, byte-wise, and leave it out of the bulk ring.
-          for (uint32_t i = 0; i < row_bytes; ++i) dst[i] = src[i];
-          valid = false;
+          for (uint32_t i = 0; i < row_bytes; ++i) d[i] = s[i];
+        } else {
+          src = reinterpret_cast<uint64_t>(s);
+          dst = reinterpret_cast<uint64_t>(d);
         }
       }
+      tab_src[idx] = src;
+      tab_dst[idx] = dst;
     }
+    __syncwarp();
+  };
+
+  // Group cursor: (batch start, rows in batch, next row in batch).
+  int32_t cur_b0 = -kBatchRows, cur_n = 0, cur_next = 0;
+
+  // Takes the next group of rows from the resolved batch (resolving the next
+  // batch first when this one is used up), merges contiguous runs and starts
+  // their loads into stage `st`.
+  auto issue_load = [&](int st) {
+    if (cur_next >= cur_n) {
+      cur_b0 += kBatchRows;
+      cur_n = min(kBatchRows, n_rows - cur_b0);
+      cur_next = 0;
+      resolve_batch(cur_b0, cur_n);
+    }
+    const int32_t count = min(b.stage_rows, cur_n - cur_next);
+    const uint8_t* src = nullptr;
+    uint8_t* dst = nullptr;
+    if (lane < count) {
+      src = reinterpret_cast<const uint8_t*>(tab_src[cur_next + lane]);
+      dst = reinterpret_cast<uint8_t*>(tab_dst[cur_next + lane]);
+    }
+    cur_next += count;
+    const bool valid = src != nullptr;
     const uint8_t* prev_src = reinterpret_cast<const uint8_t*>(
         __shfl_up_sync(0xffffffffu, reinterpret_cast<uintptr_t>(src), 1));
     uint8_t* prev_dst = reinterpret_cast<uint8_t*>(
         __shfl_up_sync(0xffffffffu, reinterpret_cast<uintptr_t>(dst), 1));
-    const bool prev_valid = __shfl_up_sync(0xffffffffu, valid ? 1 : 0, 1) != 0;
-    const bool cont = valid && lane > 0 && prev_valid && src == prev_src + row_bytes &&
+    const bool cont = valid && lane > 0 && prev_src != nullptr && src == prev_src + row_bytes &&
                       dst == prev_dst + row_bytes;
     const uint32_t cont_mask = __ballot_sync(0xffffffffu, cont);
     const bool head = valid && !cont;
@@ -368,7 +435,7 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b) {
   };
 
   int64_t issued = 0;
-  for (; issued < n_groups && issued < b.stages; ++issued) issue_load(issued, static_cast<int>(issued));
+  for (; issued < n_groups && issued < b.stages; ++issued) issue_load(static_cast<int>(issued));
 
   bool timed_out = false;
   for (int64_t g = 0; g < n_groups; ++g) {
@@ -403,7 +470,7 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b) {
     if (g >= 1 && issued < n_groups) {
       // The previous group's stage is free once its store has read it.
       bulk_wait_read_all_but_one();
-      issue_load(issued, static_cast<int>(issued % b.stages));
+      issue_load(static_cast<int>(issued % b.stages));
       ++issued;
     }
   }
@@ -442,7 +509,30 @@ BulkConfig bulk_config() {
 
 size_t bulk_smem_bytes(const BulkParams& b) {
   return static_cast<size_t>(b.stages) * b.stage_bytes + kBulkMaxStages * sizeof(uint64_t) +
-         kBulkMaxStages * 32 * (sizeof(uint64_t) + sizeof(uint32_t));
+         kBulkMaxStages * 32 * (sizeof(uint64_t) + sizeof(uint32_t)) +
+         2 * kBatchRows * sizeof(uint64_t);
+}
+
+// LMCB_PDL=0 launches without the programmatic-serialization attribute.
+bool pdl_enabled() {
+  const char* v = std::getenv("LMCB_PDL");
+  return v == nullptr || std::strcmp(v, "0") != 0;
+}
+
+template <typename Kernel, typename... Args>
+cudaError_t launch_ex(Kernel* kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                      Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
 template <typename SlotT>
@@ -453,13 +543,15 @@ cudaError_t launch_bulk(const TransferParams& p, const BulkParams& b, int mode, 
   if (mode == kPtrArray) {
     err = ensure_smem_limit<&transfer_rows_bulk_kernel<SlotT, kPtrArray>>(smem, kBulkSmemCap);
     if (err != cudaSuccess) return err;
-    transfer_rows_bulk_kernel<SlotT, kPtrArray><<<grid, 32, smem, stream>>>(p, b);
+    err = launch_ex(&transfer_rows_bulk_kernel<SlotT, kPtrArray>, dim3(grid), dim3(32), smem,
+                    stream, p, b);
   } else {
     err = ensure_smem_limit<&transfer_rows_bulk_kernel<SlotT, kDirect>>(smem, kBulkSmemCap);
     if (err != cudaSuccess) return err;
-    transfer_rows_bulk_kernel<SlotT, kDirect><<<grid, 32, smem, stream>>>(p, b);
+    err = launch_ex(&transfer_rows_bulk_kernel<SlotT, kDirect>, dim3(grid), dim3(32), smem,
+                    stream, p, b);
   }
-  return cudaGetLastError();
+  return err;
 }
 
 // True when `ptr` is device memory (not a host mapping); bulk copies are
@@ -489,11 +581,11 @@ int pick_vec(std::initializer_list<uint64_t> vals) {
 template <typename SlotT, int VEC>
 cudaError_t launch_vec(const TransferParams& p, int mode, int grid, cudaStream_t stream) {
   if (mode == kPtrArray) {
-    transfer_rows_kernel<SlotT, VEC, kPtrArray><<<grid, kThreads, 0, stream>>>(p);
-  } else {
-    transfer_rows_kernel<SlotT, VEC, kDirect><<<grid, kThreads, 0, stream>>>(p);
+    return launch_ex(&transfer_rows_kernel<SlotT, VEC, kPtrArray>, dim3(grid), dim3(kThreads), 0,
+                     stream, p);
   }
-  return cudaGetLastError();
+  return launch_ex(&transfer_rows_kernel<SlotT, VEC, kDirect>, dim3(grid), dim3(kThreads), 0,
+                   stream, p);
 }
 
 template <typename SlotT>
@@ -554,15 +646,18 @@ int launch_transfer(TransferParams p, int type, int slot_type, int mode,
   const int64_t stage_bytes = static_cast<int64_t>(bc.stage_kb) * 1024;
   const bool bulk_ok = vec == 16 && p.row_bytes % 16 == 0 && p.row_bytes <= stage_bytes &&
                        is_device_memory(p.lmc);
-  if (bulk_ok && forced != 1) {
+  const int64_t total_rows = static_cast<int64_t>(p.num_kv) * p.num_layers * p.num_tokens;
+  if (bulk_ok && forced != 1 && total_rows < (int64_t(1) << 31)) {
     BulkParams b;
-    b.num_rows = static_cast<int64_t>(p.num_kv) * p.num_layers * p.num_tokens;
+    b.num_rows = static_cast<int32_t>(total_rows);
     int64_t rows = stage_bytes / p.row_bytes;
     b.stage_rows = static_cast<int32_t>(rows > 32 ? 32 : rows);
     b.stages = bc.stages;
     b.stage_bytes = static_cast<int32_t>(stage_bytes);
+    b.div_tokens = FastDiv(static_cast<uint32_t>(p.num_tokens));
+    b.div_layers = FastDiv(static_cast<uint32_t>(p.num_layers));
     int64_t grid = static_cast<int64_t>(current_sm_count()) * bc.ctas_per_sm;
-    const int64_t groups = (b.num_rows + b.stage_rows - 1) / b.stage_rows;
+    const int64_t groups = (total_rows + b.stage_rows - 1) / b.stage_rows;
     if (grid > groups) grid = groups;
     if (grid < 1) grid = 1;
     cudaError_t err = slot_type == LMCB_DTYPE_INT64

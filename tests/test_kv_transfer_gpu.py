@@ -439,3 +439,28 @@ def test_workload_full_size(name, memobj_on, pin_alloc):
     assert c_ops.device_status(torch.cuda.current_device()) == 0
     del kv
     torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("ctas_per_sm", ["1", "3"])
+def test_large_single_launch(ctas_per_sm, monkeypatch):
+    """One launch of 262144 rows: each bulk-copy CTA resolves many 256-row
+    batches and its ring wraps many times."""
+    monkeypatch.setenv("LMCB_BULK_CTAS_PER_SM", ctas_per_sm)
+    num_layers, num_blocks, block_size, heads, hd, T = 32, 512, 16, 8, 128, 4096
+    pbs = num_blocks * block_size
+    kv = kv_list(num_layers, num_blocks, block_size, heads, hd, torch.bfloat16, seed=21)
+    slots = seeded_slots(pbs, T, seed=22, n_neg=100)
+    obj = torch.zeros([2, num_layers, T, heads * hd], dtype=torch.bfloat16, device=DEV)
+    c_ops.multi_layer_kv_transfer(obj, ptrs_of(kv), slots.to(DEV), kv[0].device, pbs, True, False)
+    kv_np = [bits(t) for t in kv]
+    want = np.zeros(obj.shape, dtype=np.int16)
+    oracle.multi_layer_kv_transfer(want, kv_np, slots.numpy(), pbs, True, False)
+    assert np.array_equal(bits(obj), want)
+    kv_new = [torch.zeros_like(t) for t in kv]
+    c_ops.multi_layer_kv_transfer(obj, ptrs_of(kv_new), slots.to(DEV), kv[0].device, pbs, False,
+                                  False)
+    new_np = [np.zeros_like(a) for a in kv_np]
+    oracle.multi_layer_kv_transfer(want, new_np, slots.numpy(), pbs, False, False)
+    for a, b in zip(kv_new, new_np):
+        assert np.array_equal(bits(a), b)
+    assert c_ops.device_status(torch.cuda.current_device()) == 0
