@@ -280,8 +280,11 @@ __device__ __forceinline__ void bulk_wait_read_all_but_one() {
   asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
 }
 
-__device__ __forceinline__ void bulk_wait_all() {
-  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+// Waits until every bulk store of this thread has finished reading shared
+// memory. The global writes themselves complete with the grid (kernel
+// completion orders them before any later work in the stream).
+__device__ __forceinline__ void bulk_wait_reads_done() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
 constexpr int kBatchRows = 256;   // rows resolved together (8 per lane)
@@ -474,7 +477,7 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b) {
       ++issued;
     }
   }
-  bulk_wait_all();
+  bulk_wait_reads_done();
 }
 
 struct BulkConfig {
