@@ -173,6 +173,32 @@ LMCB_API int lmcb_multi_layer_kv_retrieve_staged(int type, int slotType, void* s
                                         int32_t numLayers, int64_t pageBuffSize,
                                         int32_t numTokensChunk);
 
+/* Size of the staging area that lmcb_multi_layer_kv_retrieve_staged_noalloc
+ * keeps on every GPU where the library is loaded (64 MiB). */
+#define LMCB_NOALLOC_STAGING_BYTES (64u << 20)
+
+/* The staged retrieve of lmcb_multi_layer_kv_retrieve_staged for callers
+ * that cannot allocate device memory when they retrieve. Examples: an engine
+ * that reserved almost all HBM for its paged KV cache up front, or a native
+ * host without a caching allocator, where a cudaMalloc / cudaFree per chunk
+ * would synchronise the device. No reference counterpart: the reference has
+ * no staged retrieve.
+ * Instead of a caller buffer it uses a staging area of
+ * LMCB_NOALLOC_STAGING_BYTES built into the library (a device array that every
+ * GPU loading the library holds until exit); it calls no allocator.
+ * Objects larger than the area are rejected with LMCB_ERR_CAPACITY before
+ * any work is queued. The first call on each device looks up the area's
+ * device address (with that device current); make that first call before any
+ * stream capture. All calls share the one area: calls whose copies and
+ * scatters overlap on the GPU (different streams, no ordering between them)
+ * race on it, so order them, for example by issuing them on one stream.
+ * Nothing needs to be cleared between calls: each call writes every staging
+ * byte it later reads. */
+LMCB_API int lmcb_multi_layer_kv_retrieve_staged_noalloc(
+    int type, int slotType, void* stream, const uint64_t* pagedKVCaches,
+    const void* hostCacheTensor, const void* slotmappings, int64_t hiddenDims, int32_t kvs,
+    int32_t numLayers, int64_t pageBuffSize, int32_t numTokensChunk);
+
 /* Reads and clears the status word of `device` (LMCB_DEVICE_FLAG_* bits).
  * Synchronous with respect to that device's legacy default stream. */
 LMCB_API int lmcb_device_status(int device, uint32_t* flags_out);

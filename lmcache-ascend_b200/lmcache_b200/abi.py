@@ -36,6 +36,8 @@ LMCB_DEVICE_FLAG_SYMBOL_OUT_OF_RANGE = 0x2
 LMCB_DEVICE_FLAG_STREAM_OVERFLOW = 0x4
 LMCB_DEVICE_FLAG_WAIT_TIMEOUT = 0x8
 
+LMCB_NOALLOC_STAGING_BYTES = 64 << 20
+
 # name -> (restype, argtypes)
 SIGNATURES: dict[str, tuple] = {
     "lmcb_version": (c_char_p, []),
@@ -66,6 +68,11 @@ SIGNATURES: dict[str, tuple] = {
         c_int,
         [c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_int64,
          c_int32, c_int32, c_int64, c_int32],
+    ),
+    "lmcb_multi_layer_kv_retrieve_staged_noalloc": (
+        c_int,
+        [c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int32, c_int32,
+         c_int64, c_int32],
     ),
     "lmcb_device_status": (c_int, [c_int, ctypes.POINTER(c_uint32)]),
     "lmcb_host_register": (c_int, [c_void_p, c_size_t, ctypes.POINTER(c_void_p)]),
