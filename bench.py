@@ -402,7 +402,7 @@ def run_ours(args):
         }
 
     if rank == 0:
-        traffic = committed_traffic("transfer_rows_kernel", spec.name)
+        traffic = committed_traffic("transfer_rows_bulk_kernel", spec.name)
         line = {
             "metric": METRIC,
             "value": round(value, 2),
@@ -447,7 +447,7 @@ def run_ours(args):
             },
             "roofline": {
                 "bound": "hbm",
-                "kernel": "transfer_rows_kernel",
+                "kernel": "transfer_rows_bulk_kernel",
                 "achieved": round(achieved, 1),
                 "peak": peaks["hbm_gbs"],
                 "peak_source": peaks["source"],

@@ -288,6 +288,9 @@ __device__ __forceinline__ void bulk_wait_reads_done() {
 }
 
 constexpr int kBatchRows = 256;   // rows resolved together (8 per lane)
+// Bit 63 of a resolved destination marks a row that is not 16-byte aligned
+// (user-space addresses never set it).
+constexpr uint64_t kMisalignedTag = uint64_t(1) << 63;
 
 struct BulkParams {
   int32_t num_rows;      // num_kv * num_layers * num_tokens (< 2^31)
@@ -328,8 +331,6 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b) {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncwarp();
-  pdl_wait();
-  pdl_launch_dependents();
 
   // Resolves rows [b0, b0 + n) of this CTA's range into tab_src / tab_dst
   // (0 for skipped rows). All slot ids and layer bases of the batch are
@@ -376,13 +377,12 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b) {
                        static_cast<int64_t>(toks[j]) * p.lmc_token_stride;
         uint8_t* s = p.page2L ? paged : lmc;
         uint8_t* d = p.page2L ? lmc : paged;
-        if (((reinterpret_cast<uintptr_t>(s) | reinterpret_cast<uintptr_t>(d)) & 15) != 0) {
+        src = reinterpret_cast<uint64_t>(s);
+        dst = reinterpret_cast<uint64_t>(d);
+        if (((src | dst) & 15) != 0) {
           // Not 16-byte aligned (only possible through the pointer array):
-          // copy this row here, byte-wise, and leave it out of the bulk ring.
-          for (uint32_t i = 0; i < row_bytes; ++i) d[i] = s[i];
-        } else {
-          src = reinterpret_cast<uint64_t>(s);
-          dst = reinterpret_cast<uint64_t>(d);
+          // tagged here, copied byte-wise when its group is issued.
+          dst |= kMisalignedTag;
         }
       }
       tab_src[idx] = src;
@@ -409,7 +409,16 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b) {
     uint8_t* dst = nullptr;
     if (lane < count) {
       src = reinterpret_cast<const uint8_t*>(tab_src[cur_next + lane]);
-      dst = reinterpret_cast<uint8_t*>(tab_dst[cur_next + lane]);
+      const uint64_t d = tab_dst[cur_next + lane];
+      if (d & kMisalignedTag) {
+        // Rows the bulk engine cannot address (16-byte alignment) are copied
+        // byte-wise by their lane and left out of the ring.
+        uint8_t* dd = reinterpret_cast<uint8_t*>(d & ~kMisalignedTag);
+        for (uint32_t i = 0; i < row_bytes; ++i) dd[i] = src[i];
+        src = nullptr;
+      } else {
+        dst = reinterpret_cast<uint8_t*>(d);
+      }
     }
     cur_next += count;
     const bool valid = src != nullptr;
@@ -436,6 +445,21 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b) {
     s_dst[st * 32 + lane] = reinterpret_cast<uint64_t>(dst);
     s_len[st * 32 + lane] = bytes;
   };
+
+  // Under programmatic dependent launch the first batch is resolved while the
+  // previous kernel in the stream is still finishing: resolution only reads
+  // the slot mapping and the layer-base array, which no transfer kernel
+  // writes, and it touches no payload. Only slots that are bounds-checked
+  // (a known paged row count) are resolved this early; payload reads and
+  // writes all come after griddepcontrol.wait.
+  if (p.num_paged_rows > 0 && n_rows > 0) {
+    cur_b0 = 0;
+    cur_n = min(kBatchRows, n_rows);
+    cur_next = 0;
+    resolve_batch(cur_b0, cur_n);
+  }
+  pdl_wait();
+  pdl_launch_dependents();
 
   int64_t issued = 0;
   for (; issued < n_groups && issued < b.stages; ++issued) issue_load(static_cast<int>(issued));
