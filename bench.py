@@ -234,7 +234,9 @@ def run_ours(args):
     host_chunks = [c.contiguous().pin_memory() for c in wl.chunks(slots, spec.chunk_size)]
     dev_chunks = [c.to(dev) for c in host_chunks]
     n_chunks = len(dev_chunks)
-    pbs = 0 if spec.use_mla else spec.page_buffer_size
+    # The connector passes num_blocks * block_size for MLA caches too
+    # (npu_connector.py:34-37); the kernels then bound-check MLA slots as well.
+    pbs = spec.page_buffer_size
     payload = wl.payload_bytes(spec, slots)  # one direction, whole sequence
     step_payload = 2 * payload
     hbm_objs = [torch.empty(spec.memobj_shape(len(c)), dtype=torch.bfloat16, device=dev)
