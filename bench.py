@@ -445,7 +445,9 @@ def run_ours(args):
                 "by_retrieve_path": {k: round(v, 2) for k, v in e2e.items()},
                 "per_direction_gbs": dir_rates,
                 "pcie_copy_engine_gbs": pcie,
-                "frac_of_copy_engine": round(e2e[best_mode] / ((pcie["h2d"] + pcie["d2h"]) / 2), 4),
+                # per GPU: the job's e2e rate / ranks, against one GPU's copy engines
+                "frac_of_copy_engine": round(e2e[best_mode] / world /
+                                             ((pcie["h2d"] + pcie["d2h"]) / 2), 4),
             },
             "roofline": {
                 "bound": "hbm",
@@ -464,7 +466,7 @@ def run_ours(args):
                           "loop; per-launch time = replay time / launches",
             },
             "cpu_baseline": cpu,
-            "gpu_launches": args.steps * 2 * n_chunks,
+            "gpu_launches": args.steps * 2 * n_chunks * world,
             "clocks": clock_summary,
         }
         print(json.dumps(line), flush=True)
