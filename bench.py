@@ -49,6 +49,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="c2")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--component", default="transfer", choices=["transfer", "cachegen"],
+                    help="cachegen: time the CacheGen CDF / encode / decode kernels instead")
     ap.add_argument("--e2e-steps", type=int, default=None,
                     help="timed steps of the pinned-host leg (default: --steps)")
     ap.add_argument("--cpu-budget", type=float, default=15.0,
@@ -319,11 +321,39 @@ def run_ours(args):
     value_eager = sum_over_ranks(step_payload * args.steps, world) / (eager_ms / 1e3) / 1e9
     host_us_per_call = host_s / (args.steps * 2 * n_chunks) * 1e6
 
+    # Same step with all chunks of each direction in one launch
+    # (c_ops.multi_layer_kv_transfer_batched, what the connector's
+    # batched_from_gpu / batched_to_gpu issue).
+    slots_dev = slots.to(dev)
+    bounds = [0]
+    for c in host_chunks:
+        bounds.append(bounds[-1] + len(c))
+
+    def step_batched():
+        for direction in (True, False):
+            c_ops.multi_layer_kv_transfer_batched(hbm_objs, ptrs, slots_dev, bounds[:-1],
+                                                  bounds[1:], dev, pbs, direction, spec.use_mla)
+
+    for _ in range(args.warmup):
+        step_batched()
+    torch.cuda.synchronize()
+    b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    b0.record(stream)
+    for _ in range(args.steps):
+        step_batched()
+    b1.record(stream)
+    torch.cuda.synchronize()
+    batched_ms = max_over_ranks(b0.elapsed_time(b1), world)
+    value_batched = sum_over_ranks(step_payload * args.steps, world) / (batched_ms / 1e3) / 1e9
+    batched_frac = (sum(alg) * 2 * args.steps / (batched_ms / 1e3) / 1e9) / measured_peaks()["hbm_gbs"]
+
     # ---- e2e: pinned-host objects through c_ops ------------------------
     if args.skip_e2e:
         if rank == 0:
             print(json.dumps({"value": round(value, 2), "ms_per_step": round(t_ms / args.steps, 4),
                               "value_eager": round(value_eager, 2),
+                              "value_batched": round(value_batched, 2),
+                              "batched_frac": round(batched_frac, 4),
                               "host_us_per_call": round(host_us_per_call, 2),
                               "achieved": round(achieved, 1),
                               "frac": round(achieved / peaks["hbm_gbs"], 4),
@@ -431,6 +461,8 @@ def run_ours(args):
                         "each direction's chunk loop captured once and replayed as a CUDA graph",
                 "value_eager": round(value_eager, 2),
                 "host_us_per_call": round(host_us_per_call, 2),
+                "value_batched": round(value_batched, 2),
+                "batched_roofline_frac": round(batched_frac, 4),
                 "payload_bytes_per_step_per_gpu": step_payload,
                 "l2": "inputs larger than L2 (each step touches 2x payload of distinct "
                       "paged rows and LMCache objects, >126 MB)",
@@ -531,9 +563,84 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_cachegen(args):
+    """CacheGen codec on one c2-shaped chunk of quantised symbols
+    ([32 layers, 256 tokens, 1024 channels], 32 bins, a skewed distribution
+    per channel): GB/s of symbols through calculate_cdf, encode and decode,
+    and the C oracle's single-thread rate on the same input."""
+    import numpy as np
+
+    from lmcache_b200 import c_ops
+    from oracle import cachegen as cg
+
+    dev = torch.device("cuda", 0)
+    L, T, C, mb = 32, 256, 1024, 32
+    rng = np.random.default_rng(0)
+    p = np.exp(-np.arange(mb) / 4.0)
+    p /= p.sum()
+    sym = rng.choice(mb, size=(L, T, C), p=p).astype(np.uint8)
+    sym_dev = torch.from_numpy(sym.view(np.int8)).to(dev)
+    cap = 2 * T + 16
+    out = torch.zeros((L, C, cap), dtype=torch.uint8, device=dev)
+    lengths = torch.zeros((L, C), dtype=torch.int32, device=dev)
+    dec = torch.empty_like(sym_dev)
+    cdf = c_ops.calculate_cdf(sym_dev, mb)
+    c_ops.encode_fast_new(cdf, sym_dev, out, lengths)
+
+    def timed(fn, reps):
+        for _ in range(args.warmup):
+            fn()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps / 1e3
+
+    nbytes = sym.size
+    t_cdf = timed(lambda: c_ops.calculate_cdf(sym_dev, mb), args.steps)
+    t_enc = timed(lambda: c_ops.encode_fast_new(cdf, sym_dev, out, lengths), args.steps)
+    t_dec = timed(lambda: c_ops.decode_fast_new(cdf, out, lengths, dec), args.steps)
+    assert torch.equal(dec, sym_dev)
+    comp = float(lengths.sum()) / nbytes
+    cdf_np = cdf.cpu().numpy()
+    t0 = time.perf_counter()
+    streams, ln = cg.encode(cdf_np, sym, cap)
+    t_cpu_enc = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    cg.decode(cdf_np, streams, ln, T)
+    t_cpu_dec = time.perf_counter() - t0
+    line = {
+        "metric": "CacheGen codec GB/s of symbols (calculate_cdf / encode / decode)",
+        "value": round(nbytes / t_enc / 1e9, 3),
+        "unit": "GB/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "higher_is_better": True,
+        "dtype": "u8",
+        "data": "synthetic (seeded geometric-like symbol distribution)",
+        "config": {"workload": "one c2 chunk of symbols [32 layers, 256 tokens, 1024 channels], "
+                               "32 bins", "compressed_fraction": round(comp, 4)},
+        "cdf_gbs": round(nbytes / t_cdf / 1e9, 3),
+        "encode_gbs": round(nbytes / t_enc / 1e9, 3),
+        "decode_gbs": round(nbytes / t_dec / 1e9, 3),
+        "us": {"cdf": round(t_cdf * 1e6, 1), "encode": round(t_enc * 1e6, 1),
+               "decode": round(t_dec * 1e6, 1)},
+        "cpu_baseline": {"encode_gbs": round(nbytes / t_cpu_enc / 1e9, 4),
+                         "decode_gbs": round(nbytes / t_cpu_dec / 1e9, 4), "cores": 1,
+                         "kind": "port", "sample": "the C oracle on the same chunk"},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
-    if args.impl == "reference":
+    if args.component == "cachegen":
+        run_cachegen(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -124,6 +124,24 @@ LMCB_API int lmcb_multi_layer_kv_transfer_unilateral_kernel(
     int64_t hiddenDims, int32_t numLayers, int64_t pageBuffSize,
     int32_t numTokensChunk, int page2L);
 
+/* Many chunks in one launch: the objects of a request that LMCache stores or
+ * retrieves together (upstream LMCache drives them through the connector's
+ * batched_from_gpu / batched_to_gpu, one multi_layer_kv_transfer per chunk;
+ * this moves all of them with one kernel). Object i is a
+ * [kvs, numLayers, T_i, hiddenDims] LMCache object at objectPtrs[i] and
+ * holds T_i = tokenOffsets[i+1] - tokenOffsets[i] tokens whose slot ids are
+ * slotmappings[slotStarts[i] ... slotStarts[i] + T_i). Per row the result is
+ * that of lmcb_multi_layer_kv_transfer_kernel on each object in turn.
+ *   objectPtrs, tokenOffsets ([numObjects + 1], ascending, tokenOffsets[0]
+ *   = 0, tokenOffsets[numObjects] = totalTokens), slotStarts: device-readable
+ *   objectsOnDevice  1 if every object is device memory (bulk-copy path),
+ *                    0 if any is host memory (zero-copy path) */
+LMCB_API int lmcb_multi_layer_kv_transfer_batched_kernel(
+    int type, int slotType, void* stream, const uint64_t* pagedKVCaches,
+    const uint64_t* objectPtrs, const int64_t* tokenOffsets, const int64_t* slotStarts,
+    int32_t numObjects, int objectsOnDevice, const void* slotmappings, int64_t hiddenDims,
+    int32_t kvs, int32_t numLayers, int64_t pageBuffSize, int32_t totalTokens, int page2L);
+
 /* One layer, separate K and V caches.
  * Replaces kvcache_ops::single_layer_kv_transfer_kernel (csrc/mem_kernels.h:14-18),
  * launched by single_layer_kv_transfer (csrc/mem_kernels.cpp:108-152).

@@ -12,11 +12,13 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <pybind11/pybind11.h>
+#include <pybind11/stl.h>
 #include <torch/extension.h>
 
 #include <cstdlib>
 #include <cstring>
 #include <string>
+#include <vector>
 
 #include "lmcache_b200.h"
 
@@ -103,8 +105,10 @@ HostRetrievePath host_retrieve_path() {
 
 // Objects at least this large are retrieved from pinned host memory with one
 // DMA into a device staging buffer plus an HBM scatter instead of zero-copy
-// kernel reads; set from measurement on B200 (PCIe Gen5 x16).
-constexpr int64_t kDmaRetrieveMinBytes = int64_t(1) << 62;
+// kernel reads. Measured on B200 (PCIe Gen5 x16), per retrieve of one object:
+//   2 MiB: zero-copy 46.6 GB/s, DMA 39.5;   8 MiB: 50.1 vs 50.7;
+//   32 MiB: 51.1 vs 53.6;                    64 MiB: 51.3 vs 54.0.
+constexpr int64_t kDmaRetrieveMinBytes = int64_t(8) << 20;
 
 }  // namespace
 
@@ -188,6 +192,108 @@ void multi_layer_kv_transfer(torch::Tensor& key_value,             // [kv, L, T,
   check_status(lmcb_multi_layer_kv_transfer_kernel(
       dtype, slot_dtype, stream, ptrs, lmc, slots, hidden, kv_size,
       static_cast<int32_t>(num_layers), page_buffer_size, static_cast<int32_t>(num_tokens),
+      direction ? 1 : 0));
+}
+
+// All chunks of a request in one launch (an addition to the reference
+// surface; the connector's batched_from_gpu / batched_to_gpu call it).
+// key_values[i] is a [kv, L, T_i, H] object holding slot_mapping[starts[i]:
+// ends[i]]. The objects are all CUDA tensors on one device, or all pinned
+// host tensors registered with host_register. Retrieval from host objects
+// of at least kDmaRetrieveMinBytes in total copies each object into one
+// device staging buffer (one cudaMemcpyAsync per object) and scatters from
+// there.
+void multi_layer_kv_transfer_batched(const std::vector<torch::Tensor>& key_values,
+                                     const torch::Tensor& key_value_ptrs,
+                                     const torch::Tensor& slot_mapping,
+                                     const std::vector<int64_t>& starts,
+                                     const std::vector<int64_t>& ends,
+                                     const torch::Device& paged_memory_device,
+                                     const int64_t page_buffer_size, const bool direction,
+                                     const bool use_mla) {
+  const int64_t n = static_cast<int64_t>(key_values.size());
+  TORCH_CHECK(static_cast<int64_t>(starts.size()) == n && static_cast<int64_t>(ends.size()) == n,
+              "starts and ends must have one entry per object");
+  if (n == 0) return;
+  TORCH_CHECK(key_value_ptrs.scalar_type() == at::ScalarType::Long,
+              "key_value_ptrs must be int64");
+  const int kv_size = use_mla ? 1 : 2;
+  const auto& first = key_values[0];
+  TORCH_CHECK(first.dim() >= 3, "key_values must be [kv, num_layers, num_tokens, hidden]");
+  const int64_t num_layers = first.size(1);
+  const int64_t hidden = first.size(-1);
+  const bool on_device = first.is_cuda();
+  TORCH_CHECK(key_value_ptrs.numel() >= num_layers, "key_value_ptrs has fewer than ",
+              num_layers, " entries");
+  const int dtype = to_lmcb_dtype(first.scalar_type());
+  const int slot_dtype = to_slot_dtype(slot_mapping.scalar_type());
+  int64_t total = 0;
+  for (int64_t i = 0; i < n; ++i) {
+    const auto& t = key_values[i];
+    TORCH_CHECK(t.scalar_type() == first.scalar_type() && t.size(1) == num_layers &&
+                    t.size(-1) == hidden && t.is_cuda() == on_device,
+                "key_values must share dtype, layer count, hidden size and residency");
+    TORCH_CHECK(t.is_contiguous(), "key_values must be contiguous");
+    TORCH_CHECK(0 <= starts[i] && starts[i] <= ends[i] && ends[i] <= slot_mapping.size(0),
+                "object ", i, ": slot range out of bounds");
+    TORCH_CHECK(t.numel() >= kv_size * num_layers * (ends[i] - starts[i]) * hidden, "object ",
+                i, " is smaller than its slot range");
+    total += ends[i] - starts[i];
+  }
+  if (total == 0) return;
+  TORCH_CHECK(total < (int64_t(1) << 31), "too many tokens in one batch");
+
+  const c10::OptionalDeviceGuard device_guard(paged_memory_device);
+  cudaStream_t stream = current_stream();
+  const auto dev = torch::Device(torch::kCUDA, c10::cuda::current_device());
+  const uint64_t* ptrs = static_cast<const uint64_t*>(get_kernel_ptr(key_value_ptrs));
+  const void* slots = get_kernel_ptr(slot_mapping);
+  const int64_t esz = first.element_size();
+
+  bool staged = false;
+  torch::Tensor staging;
+  if (!on_device && !direction) {
+    const int64_t bytes = kv_size * num_layers * total * hidden * esz;
+    const HostRetrievePath path = host_retrieve_path();
+    staged = path == HostRetrievePath::kDma ||
+             (path == HostRetrievePath::kAuto && bytes >= kDmaRetrieveMinBytes);
+    if (staged) {
+      staging = torch::empty({bytes}, torch::TensorOptions().dtype(torch::kUInt8).device(dev));
+    }
+  }
+
+  // Object table: [ptrs (n) | token offsets (n + 1) | slot starts (n)].
+  auto table = torch::empty({3 * n + 1},
+                            torch::TensorOptions().dtype(torch::kLong).pinned_memory(true));
+  int64_t* tab = table.data_ptr<int64_t>();
+  int64_t off = 0, staged_off = 0;
+  for (int64_t i = 0; i < n; ++i) {
+    const int64_t count = ends[i] - starts[i];
+    const int64_t obj_bytes = kv_size * num_layers * count * hidden * esz;
+    void* obj;
+    if (staged) {
+      obj = static_cast<uint8_t*>(staging.data_ptr()) + staged_off;
+      if (obj_bytes > 0) {
+        auto dst = staging.narrow(0, staged_off, obj_bytes);
+        dst.copy_(key_values[i].view(torch::kUInt8).reshape({-1}).narrow(0, 0, obj_bytes),
+                  /*non_blocking=*/true);
+      }
+      staged_off += (obj_bytes + 255) / 256 * 256;
+    } else {
+      obj = get_kernel_ptr(key_values[i]);
+    }
+    tab[i] = reinterpret_cast<int64_t>(obj);
+    tab[n + i] = off;
+    tab[2 * n + 1 + i] = starts[i];
+    off += count;
+  }
+  tab[2 * n] = off;
+  auto table_dev = table.to(dev, /*non_blocking=*/true);
+  const int64_t* td = table_dev.data_ptr<int64_t>();
+  check_status(lmcb_multi_layer_kv_transfer_batched_kernel(
+      dtype, slot_dtype, stream, ptrs, reinterpret_cast<const uint64_t*>(td), td + n,
+      td + 2 * n + 1, static_cast<int32_t>(n), (on_device || staged) ? 1 : 0, slots, hidden,
+      kv_size, static_cast<int32_t>(num_layers), page_buffer_size, static_cast<int32_t>(total),
       direction ? 1 : 0));
 }
 
@@ -431,6 +537,7 @@ PYBIND11_MODULE(c_ops, m) {
   m.def("calculate_cdf", &calculate_cdf);
   m.def("rotary_embedding_k_fused", &rotary_embedding_k_fused);
   // Additions beyond the reference surface.
+  m.def("multi_layer_kv_transfer_batched", &multi_layer_kv_transfer_batched);
   m.def("host_unregister", &unregister_memory);
   m.def("get_device_ptr", &get_device_ptr);
   m.def("device_status", &device_status);

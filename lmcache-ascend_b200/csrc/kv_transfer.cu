@@ -41,11 +41,13 @@ constexpr int kMaxTileRows = 128;
 constexpr int kUnroll = 4;
 constexpr int kTargetTileBytes = 32 * 1024;
 
-// How paged-side row addresses are formed.
-//   kPtrArray: base = ptrs_k[layer] (kv == 0) or ptrs_v[layer] (kv == 1),
-//              plus kv * page_kv_offset.
-//   kDirect:   base = base_k (kv == 0) or base_v (kv == 1).
-enum PagedMode { kPtrArray = 0, kDirect = 1 };
+// How row addresses are formed.
+//   kPtrArray: paged base = ptrs_k[layer] (kv == 0) or ptrs_v[layer]
+//              (kv == 1), plus kv * page_kv_offset; one LMCache object.
+//   kDirect:   paged base = base_k (kv == 0) or base_v (kv == 1); one object.
+//   kBatched:  paged side as kPtrArray; many LMCache objects, located through
+//              the object table (see TransferParams::obj_*).
+enum PagedMode { kPtrArray = 0, kDirect = 1, kBatched = 2 };
 
 struct TransferParams {
   // LMCache side: row(kv, layer, t) = lmc + kv*lmc_kv_stride
@@ -74,7 +76,38 @@ struct TransferParams {
   FastDiv row_vecs;        // row_bytes / VEC
   int32_t page2L;          // 1: paged -> LMCache, 0: LMCache -> paged
   unsigned int* status;
+  // kBatched only. Tokens t are numbered across all objects: object i holds
+  // t in [obj_offsets[i], obj_offsets[i+1]) (num_objects + 1 prefix sums),
+  // laid out [kv, num_layers, T_i, hidden] at obj_ptrs[i], and takes its slot
+  // ids from slots[obj_slot_starts[i] + (t - obj_offsets[i])].
+  const uint64_t* obj_ptrs;
+  const int64_t* obj_offsets;
+  const int64_t* obj_slot_starts;
+  int32_t num_objects;
 };
+
+// LMCache-side row address of (kv, layer, t) and the index of t's slot id.
+template <int MODE>
+__device__ __forceinline__ uint8_t* lmc_row(const TransferParams& p, int kv, int layer, int t,
+                                            int64_t* slot_index) {
+  if (MODE == kBatched) {
+    // Last object whose first token is <= t (empty objects are skipped over).
+    int lo = 0, hi = p.num_objects;  // obj_offsets[lo] <= t < obj_offsets[hi]
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (__ldg(p.obj_offsets + mid) <= t) lo = mid; else hi = mid;
+    }
+    const int64_t first = __ldg(p.obj_offsets + lo);
+    const int64_t count = __ldg(p.obj_offsets + lo + 1) - first;
+    const int64_t j = t - first;
+    *slot_index = __ldg(p.obj_slot_starts + lo) + j;
+    return reinterpret_cast<uint8_t*>(__ldg(p.obj_ptrs + lo)) +
+           ((static_cast<int64_t>(kv) * p.num_layers + layer) * count + j) * p.row_bytes;
+  }
+  *slot_index = t;
+  return p.lmc + kv * p.lmc_kv_stride + layer * p.lmc_layer_stride +
+         static_cast<int64_t>(t) * p.lmc_token_stride;
+}
 
 template <int VEC>
 struct VecType;
@@ -125,7 +158,9 @@ transfer_rows_kernel(const TransferParams p) {
     uint8_t* dst = nullptr;
     if (tid < n_tile) {
       const int t = t0 + tid;
-      const int64_t slot = static_cast<int64_t>(slots[t]);
+      int64_t slot_index;
+      uint8_t* lmc = lmc_row<MODE>(p, kv, layer, t, &slot_index);
+      const int64_t slot = static_cast<int64_t>(slots[slot_index]);
       valid = slot >= 0;
       if (valid && p.num_paged_rows > 0 && slot >= p.num_paged_rows) {
         valid = false;
@@ -133,15 +168,13 @@ transfer_rows_kernel(const TransferParams p) {
       }
       if (valid) {
         uint8_t* paged;
-        if (MODE == kPtrArray) {
+        if (MODE != kDirect) {
           const uint64_t* arr = kv == 0 ? p.ptrs_k : p.ptrs_v;
           paged = reinterpret_cast<uint8_t*>(arr[layer]) + kv * p.page_kv_offset;
         } else {
           paged = kv == 0 ? p.base_k : p.base_v;
         }
         paged += slot * p.paged_row_stride;
-        uint8_t* lmc = p.lmc + kv * p.lmc_kv_stride + layer * p.lmc_layer_stride +
-                       static_cast<int64_t>(t) * p.lmc_token_stride;
         if (p.page2L) {
           src = paged;
           dst = lmc;
@@ -339,25 +372,27 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b) {
     constexpr int kPer = kBatchRows / 32;
     int64_t slot[kPer];
     uint8_t* base[kPer];
-    int kvs[kPer], layers[kPer], toks[kPer];
+    uint8_t* lmcs[kPer];
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
       const int idx = lane + 32 * j;
       slot[j] = -1;
       base[j] = nullptr;
-      kvs[j] = layers[j] = toks[j] = 0;
+      lmcs[j] = nullptr;
       if (idx < n) {
         const uint32_t r = static_cast<uint32_t>(r_begin + b0 + idx);
         const uint32_t q = b.div_tokens.div(r);
-        toks[j] = static_cast<int>(r - q * b.div_tokens.d);
-        kvs[j] = static_cast<int>(b.div_layers.div(q));
-        layers[j] = static_cast<int>(q - kvs[j] * b.div_layers.d);
-        slot[j] = static_cast<int64_t>(slots[toks[j]]);
-        if (MODE == kPtrArray) {
-          const uint64_t* arr = kvs[j] == 0 ? p.ptrs_k : p.ptrs_v;
-          base[j] = reinterpret_cast<uint8_t*>(arr[layers[j]]) + kvs[j] * p.page_kv_offset;
+        const int tok = static_cast<int>(r - q * b.div_tokens.d);
+        const int kv = static_cast<int>(b.div_layers.div(q));
+        const int layer = static_cast<int>(q - kv * b.div_layers.d);
+        int64_t slot_index;
+        lmcs[j] = lmc_row<MODE>(p, kv, layer, tok, &slot_index);
+        slot[j] = static_cast<int64_t>(slots[slot_index]);
+        if (MODE != kDirect) {
+          const uint64_t* arr = kv == 0 ? p.ptrs_k : p.ptrs_v;
+          base[j] = reinterpret_cast<uint8_t*>(arr[layer]) + kv * p.page_kv_offset;
         } else {
-          base[j] = kvs[j] == 0 ? p.base_k : p.base_v;
+          base[j] = kv == 0 ? p.base_k : p.base_v;
         }
       }
     }
@@ -373,10 +408,8 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b) {
       }
       if (valid) {
         uint8_t* paged = base[j] + slot[j] * p.paged_row_stride;
-        uint8_t* lmc = p.lmc + kvs[j] * p.lmc_kv_stride + layers[j] * p.lmc_layer_stride +
-                       static_cast<int64_t>(toks[j]) * p.lmc_token_stride;
-        uint8_t* s = p.page2L ? paged : lmc;
-        uint8_t* d = p.page2L ? lmc : paged;
+        uint8_t* s = p.page2L ? paged : lmcs[j];
+        uint8_t* d = p.page2L ? lmcs[j] : paged;
         src = reinterpret_cast<uint64_t>(s);
         dst = reinterpret_cast<uint64_t>(d);
         if (((src | dst) & 15) != 0) {
@@ -562,23 +595,24 @@ cudaError_t launch_ex(Kernel* kernel, dim3 grid, dim3 block, size_t smem, cudaSt
   return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
+template <typename SlotT, int MODE>
+cudaError_t launch_bulk_mode(const TransferParams& p, const BulkParams& b, int grid,
+                             cudaStream_t stream) {
+  const size_t smem = bulk_smem_bytes(b);
+  cudaError_t err = ensure_smem_limit<&transfer_rows_bulk_kernel<SlotT, MODE>>(smem, kBulkSmemCap);
+  if (err != cudaSuccess) return err;
+  return launch_ex(&transfer_rows_bulk_kernel<SlotT, MODE>, dim3(grid), dim3(32), smem, stream,
+                   p, b);
+}
+
 template <typename SlotT>
 cudaError_t launch_bulk(const TransferParams& p, const BulkParams& b, int mode, int grid,
                         cudaStream_t stream) {
-  const size_t smem = bulk_smem_bytes(b);
-  cudaError_t err;
-  if (mode == kPtrArray) {
-    err = ensure_smem_limit<&transfer_rows_bulk_kernel<SlotT, kPtrArray>>(smem, kBulkSmemCap);
-    if (err != cudaSuccess) return err;
-    err = launch_ex(&transfer_rows_bulk_kernel<SlotT, kPtrArray>, dim3(grid), dim3(32), smem,
-                    stream, p, b);
-  } else {
-    err = ensure_smem_limit<&transfer_rows_bulk_kernel<SlotT, kDirect>>(smem, kBulkSmemCap);
-    if (err != cudaSuccess) return err;
-    err = launch_ex(&transfer_rows_bulk_kernel<SlotT, kDirect>, dim3(grid), dim3(32), smem,
-                    stream, p, b);
+  switch (mode) {
+    case kPtrArray: return launch_bulk_mode<SlotT, kPtrArray>(p, b, grid, stream);
+    case kDirect: return launch_bulk_mode<SlotT, kDirect>(p, b, grid, stream);
+    default: return launch_bulk_mode<SlotT, kBatched>(p, b, grid, stream);
   }
-  return err;
 }
 
 // True when `ptr` is device memory (not a host mapping); bulk copies are
@@ -607,12 +641,17 @@ int pick_vec(std::initializer_list<uint64_t> vals) {
 
 template <typename SlotT, int VEC>
 cudaError_t launch_vec(const TransferParams& p, int mode, int grid, cudaStream_t stream) {
-  if (mode == kPtrArray) {
-    return launch_ex(&transfer_rows_kernel<SlotT, VEC, kPtrArray>, dim3(grid), dim3(kThreads), 0,
-                     stream, p);
+  switch (mode) {
+    case kPtrArray:
+      return launch_ex(&transfer_rows_kernel<SlotT, VEC, kPtrArray>, dim3(grid), dim3(kThreads),
+                       0, stream, p);
+    case kDirect:
+      return launch_ex(&transfer_rows_kernel<SlotT, VEC, kDirect>, dim3(grid), dim3(kThreads), 0,
+                       stream, p);
+    default:
+      return launch_ex(&transfer_rows_kernel<SlotT, VEC, kBatched>, dim3(grid), dim3(kThreads),
+                       0, stream, p);
   }
-  return launch_ex(&transfer_rows_kernel<SlotT, VEC, kDirect>, dim3(grid), dim3(kThreads), 0,
-                   stream, p);
 }
 
 template <typename SlotT>
@@ -631,7 +670,7 @@ cudaError_t launch_slot(const TransferParams& p, int vec, int mode, int grid,
 // must all be multiples of the vector width.
 int launch_transfer(TransferParams p, int type, int slot_type, int mode,
                     std::initializer_list<uint64_t> alignment_terms,
-                    cudaStream_t stream, const char* who) {
+                    cudaStream_t stream, const char* who, bool objects_on_device = false) {
   const int esz = dtype_size(type);
   if (esz == 0) {
     return fail(LMCB_ERR_UNSUPPORTED_DTYPE, std::string(who) + ": ScalarType not supported.");
@@ -644,10 +683,15 @@ int launch_transfer(TransferParams p, int type, int slot_type, int mode,
     return fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": negative size.");
   }
   if (p.num_tokens == 0 || p.num_layers == 0) return LMCB_OK;
-  if (p.lmc == nullptr || p.slots == nullptr) {
+  if ((mode != kBatched && p.lmc == nullptr) || p.slots == nullptr) {
     return fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": NULL pointer.");
   }
-  if (mode == kPtrArray && (p.ptrs_k == nullptr || p.ptrs_v == nullptr)) {
+  if (mode == kBatched &&
+      (p.obj_ptrs == nullptr || p.obj_offsets == nullptr || p.obj_slot_starts == nullptr ||
+       p.num_objects <= 0)) {
+    return fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": NULL object table.");
+  }
+  if (mode != kDirect && (p.ptrs_k == nullptr || p.ptrs_v == nullptr)) {
     return fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": NULL pointer array.");
   }
   if (mode == kDirect && (p.base_k == nullptr || (p.num_kv > 1 && p.base_v == nullptr))) {
@@ -671,8 +715,9 @@ int launch_transfer(TransferParams p, int type, int slot_type, int mode,
   }();
   const BulkConfig bc = bulk_config();
   const int64_t stage_bytes = static_cast<int64_t>(bc.stage_kb) * 1024;
+  const bool lmc_on_device = mode == kBatched ? objects_on_device : is_device_memory(p.lmc);
   const bool bulk_ok = vec == 16 && p.row_bytes % 16 == 0 && p.row_bytes <= stage_bytes &&
-                       is_device_memory(p.lmc);
+                       lmc_on_device;
   const int64_t total_rows = static_cast<int64_t>(p.num_kv) * p.num_layers * p.num_tokens;
   if (bulk_ok && forced != 1 && total_rows < (int64_t(1) << 31)) {
     BulkParams b;
@@ -883,6 +928,47 @@ int lmcb_load_and_reshape_flash_kernel(int type, int slotType, void* stream,
        reinterpret_cast<uint64_t>(keyCachePtr), reinterpret_cast<uint64_t>(valueCachePtr),
        static_cast<uint64_t>(p.paged_row_stride)},
       static_cast<cudaStream_t>(stream), who);
+}
+
+int lmcb_multi_layer_kv_transfer_batched_kernel(
+    int type, int slotType, void* stream, const uint64_t* pagedKVCaches,
+    const uint64_t* objectPtrs, const int64_t* tokenOffsets, const int64_t* slotStarts,
+    int32_t numObjects, int objectsOnDevice, const void* slotmappings, int64_t hiddenDims,
+    int32_t kvs, int32_t numLayers, int64_t pageBuffSize, int32_t totalTokens, int page2L) {
+  lmcb::clear_error();
+  const char* who = "multi_layer_kv_transfer_batched";
+  if (kvs != 1 && kvs != 2) {
+    return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": kvs must be 1 or 2.");
+  }
+  if (kvs == 2 && pageBuffSize <= 0) {
+    return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT,
+                      std::string(who) + ": page_buffer_size must be positive for K/V caches.");
+  }
+  if (numObjects < 0) {
+    return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": negative object count.");
+  }
+  if (numObjects == 0 || totalTokens == 0) return LMCB_OK;
+  const int64_t esz = lmcb::dtype_size(type);
+  const int64_t row = hiddenDims * esz;
+  TransferParams p{};
+  p.ptrs_k = pagedKVCaches;
+  p.ptrs_v = pagedKVCaches;
+  p.page_kv_offset = pageBuffSize * row;
+  p.paged_row_stride = row;
+  p.num_paged_rows = pageBuffSize;
+  p.slots = slotmappings;
+  p.num_tokens = totalTokens;
+  p.num_layers = numLayers;
+  p.num_kv = kvs;
+  p.row_bytes = esz == 0 ? 1 : row;
+  p.page2L = page2L ? 1 : 0;
+  p.obj_ptrs = objectPtrs;
+  p.obj_offsets = tokenOffsets;
+  p.obj_slot_starts = slotStarts;
+  p.num_objects = numObjects;
+  return lmcb::launch_transfer(p, type, slotType, lmcb::kBatched,
+                               {static_cast<uint64_t>(row), static_cast<uint64_t>(p.page_kv_offset)},
+                               static_cast<cudaStream_t>(stream), who, objectsOnDevice != 0);
 }
 
 int lmcb_multi_layer_kv_retrieve_staged(int type, int slotType, void* stream,

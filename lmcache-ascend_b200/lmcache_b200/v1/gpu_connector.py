@@ -92,6 +92,39 @@ class VLLMPagedMemGPUConnectorV2:
             # A host object must hold the data when the call returns.
             torch.cuda.current_stream().synchronize()
 
+    def _batched(self, memory_objs: Sequence[MemoryObj], starts: Sequence[int],
+                 ends: Sequence[int], direction: bool, **kwargs) -> None:
+        if "kvcaches" not in kwargs:
+            raise ValueError("'kvcaches' should be provided in kwargs.")
+        if "slot_mapping" not in kwargs:
+            raise ValueError("'slot_mapping' should be provided in kwargs.")
+        kvcaches: List[torch.Tensor] = kwargs["kvcaches"]
+        slot_mapping: torch.Tensor = kwargs["slot_mapping"]
+        ptrs = self._initialize_pointers(kvcaches)
+        # One launch per residency group (device objects / pinned host objects).
+        groups: Dict[bool, list] = {}
+        for obj, s, e in zip(memory_objs, starts, ends):
+            assert obj.tensor is not None
+            groups.setdefault(obj.tensor.is_cuda, []).append((obj.tensor, int(s), int(e)))
+        for items in groups.values():
+            c_ops.multi_layer_kv_transfer_batched(
+                [t for t, _, _ in items], ptrs, slot_mapping, [s for _, s, _ in items],
+                [e for _, _, e in items], kvcaches[0].device, self.page_buffer_size, direction,
+                self.use_mla)
+        if False in groups:
+            torch.cuda.current_stream().synchronize()
+
+    def batched_from_gpu(self, memory_objs: Sequence[MemoryObj], starts: Sequence[int],
+                         ends: Sequence[int], **kwargs) -> None:
+        """Store several chunks with one kernel launch (upstream LMCache calls
+        ``from_gpu`` once per chunk here)."""
+        self._batched(memory_objs, starts, ends, True, **kwargs)
+
+    def batched_to_gpu(self, memory_objs: Sequence[MemoryObj], starts: Sequence[int],
+                       ends: Sequence[int], **kwargs) -> None:
+        """Load several chunks back with one kernel launch."""
+        self._batched(memory_objs, starts, ends, False, **kwargs)
+
     def from_gpu(self, memory_obj: MemoryObj, start: int, end: int, **kwargs) -> None:
         """Store tokens [start, end) of the paged cache into ``memory_obj``."""
         self._transfer(memory_obj, start, end, True, **kwargs)
