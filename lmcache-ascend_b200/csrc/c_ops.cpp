@@ -258,7 +258,14 @@ void multi_layer_kv_transfer_batched(const std::vector<torch::Tensor>& key_value
     staged = path == HostRetrievePath::kDma ||
              (path == HostRetrievePath::kAuto && bytes >= kDmaRetrieveMinBytes);
     if (staged) {
-      staging = torch::empty({bytes}, torch::TensorOptions().dtype(torch::kUInt8).device(dev));
+      // Each object starts on a 256-byte boundary of the staging buffer.
+      int64_t staging_bytes = 0;
+      for (int64_t i = 0; i < n; ++i) {
+        const int64_t obj_bytes = kv_size * num_layers * (ends[i] - starts[i]) * hidden * esz;
+        staging_bytes += (obj_bytes + 255) / 256 * 256;
+      }
+      staging = torch::empty({staging_bytes},
+                             torch::TensorOptions().dtype(torch::kUInt8).device(dev));
     }
   }
 
@@ -270,8 +277,9 @@ void multi_layer_kv_transfer_batched(const std::vector<torch::Tensor>& key_value
   for (int64_t i = 0; i < n; ++i) {
     const int64_t count = ends[i] - starts[i];
     const int64_t obj_bytes = kv_size * num_layers * count * hidden * esz;
-    void* obj;
-    if (staged) {
+    void* obj = nullptr;  // empty objects hold no token; their address is never used
+    if (count == 0) {
+    } else if (staged) {
       obj = static_cast<uint8_t*>(staging.data_ptr()) + staged_off;
       if (obj_bytes > 0) {
         auto dst = staging.narrow(0, staged_off, obj_bytes);

@@ -112,6 +112,9 @@ def test_connector_batched_round_trip(arena):
     conn = VLLMPagedMemGPUConnectorV2(spec.hidden, spec.num_layers)
     starts, ends = [0, 100, 200], [100, 200, 256]
     objs = [arena.allocate(conn.get_shape(e - s), torch.bfloat16) for s, e in zip(starts, ends)]
+    for mo in objs:
+        mo.tensor.zero_()  # rows of skipped slots keep these zeros
+    arena.free(objs[1])
     objs[1] = type(objs[0])(torch.zeros(conn.get_shape(100), dtype=torch.bfloat16, device=DEV),
                             0, 0)  # one HBM object among host objects
     conn.batched_from_gpu(objs, starts, ends, kvcaches=kv, slot_mapping=sd)
