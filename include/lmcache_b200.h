@@ -71,6 +71,7 @@ typedef enum {
 #define LMCB_DEVICE_FLAG_SYMBOL_OUT_OF_RANGE 0x2u
 #define LMCB_DEVICE_FLAG_STREAM_OVERFLOW 0x4u
 #define LMCB_DEVICE_FLAG_WAIT_TIMEOUT 0x8u
+#define LMCB_DEVICE_FLAG_POSITION_OUT_OF_RANGE 0x10u
 
 /* Library version, "major.minor.patch". */
 LMCB_API const char* lmcb_version(void);
@@ -296,6 +297,30 @@ LMCB_API int lmcb_decode_prefsum(const int16_t* cdf, const uint8_t* bytestreams,
                                  int64_t streamBytes, const int64_t* endOffsets,
                                  int8_t* output, int32_t numLayers, int32_t numTokens,
                                  int32_t numChannels, int32_t maxBins, void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* CacheBlend: fused K re-rotation                                            */
+/* ------------------------------------------------------------------------- */
+
+/* Replaces rotary_embedding_k_fused (csrc/pos_kernels.h:7-10; unimplemented
+ * in the reference, csrc/pos_kernels.cpp:7-14). Rotates, in place, the rotary
+ * dims of every head of every token of `key` from the angles of
+ * oldPositions[t] to those of newPositions[t]: the same result as undoing the
+ * rotary embedding at the old position and applying it at the new one, with
+ * one rounding to the key's type.
+ *   key          [numTokens, numHeads, headSize] elements of keyType; tokens
+ *                keyTokenStride elements apart, heads headSize apart
+ *   cosSinCache  [maxPosition, rotDim] of cacheType, each row [cos | sin]
+ *   isNeox       non-zero: pairs (i, i + rotDim/2); zero: pairs (2i, 2i + 1)
+ * Positions outside [0, maxPosition) leave their token unchanged and set
+ * LMCB_DEVICE_FLAG_POSITION_OUT_OF_RANGE. */
+LMCB_API int lmcb_rotary_embedding_k_fused(const void* oldPositions, const void* newPositions,
+                                           int posType, void* key, int keyType,
+                                           int64_t numTokens, int64_t numHeads,
+                                           int64_t headSize, int64_t keyTokenStride,
+                                           const void* cosSinCache, int cacheType,
+                                           int64_t rotDim, int64_t maxPosition, int isNeox,
+                                           void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -29,7 +29,8 @@ BUILD = os.path.join(REPO, "_build")
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 
-CU_SOURCES = ["common.cu", "kv_transfer.cu", "host_mem.cu", "cachegen.cu", "noalloc.cu"]
+CU_SOURCES = ["common.cu", "kv_transfer.cu", "host_mem.cu", "cachegen.cu", "noalloc.cu",
+              "pos_kernels.cu"]
 HEADERS = [os.path.join(CSRC, "common.cuh"), os.path.join(INCLUDE, "lmcache_b200.h")]
 LIB = os.path.join(PKG, "liblmcache_b200.so")
 EXT = os.path.join(PKG, "c_ops" + sysconfig.get_config_var("EXT_SUFFIX"))

@@ -515,15 +515,43 @@ void decode_cuda_prefsum(const at::Tensor& cdf, const at::Tensor& bytestreams,
 }
 
 // ---------------------------------------------------------------------------
-// Fused rotary (csrc/pos_kernels.cpp:7-14): unimplemented in the reference.
+// Fused rotary (csrc/pos_kernels.h:7-10; unimplemented in the reference)
 // ---------------------------------------------------------------------------
 
 void rotary_embedding_k_fused(const torch::Tensor& old_positions,
                               const torch::Tensor& new_positions, torch::Tensor& key,
                               int64_t head_size, const torch::Tensor& cos_sin_cache,
                               bool is_neox) {
-  PyErr_SetString(PyExc_NotImplementedError, "Please contact LMCache Ascend.");
-  throw py::error_already_set();
+  TORCH_CHECK(key.is_cuda() && old_positions.is_cuda() && new_positions.is_cuda() &&
+                  cos_sin_cache.is_cuda(),
+              "rotary_embedding_k_fused: all tensors must be CUDA tensors");
+  TORCH_CHECK(key.dim() >= 2, "key must be [num_tokens, num_heads * head_size] or "
+                              "[num_tokens, num_heads, head_size]");
+  const int64_t num_tokens = key.size(0);
+  TORCH_CHECK(old_positions.numel() == num_tokens && new_positions.numel() == num_tokens,
+              "positions must have one entry per token");
+  TORCH_CHECK(old_positions.scalar_type() == new_positions.scalar_type(),
+              "old and new positions must have the same dtype");
+  TORCH_CHECK(old_positions.is_contiguous() && new_positions.is_contiguous(),
+              "positions must be contiguous");
+  TORCH_CHECK(cos_sin_cache.dim() == 2 && cos_sin_cache.is_contiguous(),
+              "cos_sin_cache must be a contiguous [max_position, rot_dim] tensor");
+  // Everything after the token dimension must be dense.
+  int64_t row = 1;
+  for (int64_t d = key.dim() - 1; d >= 1; --d) {
+    TORCH_CHECK(key.size(d) == 1 || key.stride(d) == row, "key rows must be contiguous");
+    row *= key.size(d);
+  }
+  TORCH_CHECK(head_size > 0 && row % head_size == 0,
+              "head_size does not divide the key row");
+  const int pos_type = to_slot_dtype(old_positions.scalar_type());
+  const c10::cuda::CUDAGuard guard(key.device());
+  check_status(lmcb_rotary_embedding_k_fused(
+      old_positions.data_ptr(), new_positions.data_ptr(), pos_type, key.data_ptr(),
+      to_lmcb_dtype(key.scalar_type()), num_tokens, row / head_size, head_size,
+      num_tokens > 1 ? key.stride(0) : row, cos_sin_cache.data_ptr(),
+      to_lmcb_dtype(cos_sin_cache.scalar_type()), cos_sin_cache.size(1),
+      cos_sin_cache.size(0), is_neox ? 1 : 0, current_stream()));
 }
 
 uint32_t device_status(int device) {

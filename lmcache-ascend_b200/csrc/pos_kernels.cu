@@ -1,0 +1,174 @@
+// pos_kernels.cu -- fused K re-rotation for CacheBlend (rotary_embedding_k_fused).
+//
+// The reference exports rotary_embedding_k_fused (csrc/pybind.cpp:25) but its
+// body raises NotImplementedError (csrc/pos_kernels.cpp:7-14). Its caller
+// (lmcache_ascend/v1/blend/positional_encoding.py:57-77) moves cached K rows
+// from the positions they were encoded at to new positions; the unfused
+// equivalent there (DummyFusedRope, :80-101) undoes the rotary embedding at
+// the old positions and applies it at the new ones. This kernel does both in
+// one pass: for each rotated pair (x1, x2) with angles a (old) and b (new),
+//   (x1, x2) <- R(b - a) (x1, x2),
+//   cos(b - a) = cos b cos a + sin b sin a,  sin(b - a) = sin b cos a - cos b sin a,
+// in fp32, rounding once to the key's type. Pairs follow the rotary layouts
+// of the cos/sin cache [max_position, rot_dim] = [cos | sin]: neox style pairs
+// dims (i, i + rot_dim/2), GPT-J style pairs (2i, 2i + 1); dims at and beyond
+// rot_dim are left unchanged.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "common.cuh"
+#include "lmcache_b200.h"
+
+namespace lmcb {
+namespace {
+
+constexpr int kRopeThreads = 128;
+
+template <typename T> __device__ __forceinline__ float to_f(T v);
+template <> __device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+template <> __device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+
+template <typename T> __device__ __forceinline__ T from_f(float v);
+template <> __device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+template <> __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
+
+struct RopeParams {
+  const void* old_pos;
+  const void* new_pos;
+  void* key;
+  const void* cache;
+  int64_t num_tokens;
+  int64_t num_heads;
+  int64_t head_size;
+  int64_t token_stride;  // elements between consecutive tokens of `key`
+  int64_t rot_dim;
+  int64_t max_position;
+  int is_neox;
+  unsigned int* status;
+};
+
+template <typename KeyT, typename CacheT, typename PosT>
+__global__ void __launch_bounds__(kRopeThreads) rope_k_fused_kernel(const RopeParams p) {
+  const int64_t token = blockIdx.x;
+  if (token >= p.num_tokens) return;
+  const int64_t a = static_cast<int64_t>(static_cast<const PosT*>(p.old_pos)[token]);
+  const int64_t b = static_cast<int64_t>(static_cast<const PosT*>(p.new_pos)[token]);
+  if (a < 0 || a >= p.max_position || b < 0 || b >= p.max_position) {
+    if (threadIdx.x == 0) raise_flag(p.status, LMCB_DEVICE_FLAG_POSITION_OUT_OF_RANGE);
+    return;
+  }
+  const int64_t half = p.rot_dim / 2;
+  const CacheT* ca = static_cast<const CacheT*>(p.cache) + a * p.rot_dim;
+  const CacheT* cb = static_cast<const CacheT*>(p.cache) + b * p.rot_dim;
+  KeyT* k = static_cast<KeyT*>(p.key) + token * p.token_stride;
+  const int64_t pairs = p.num_heads * half;
+  for (int64_t q = threadIdx.x; q < pairs; q += blockDim.x) {
+    const int64_t h = q / half;
+    const int64_t i = q - h * half;
+    const float cos_a = to_f(ca[i]), sin_a = to_f(ca[half + i]);
+    const float cos_b = to_f(cb[i]), sin_b = to_f(cb[half + i]);
+    const float c = cos_b * cos_a + sin_b * sin_a;
+    const float s = sin_b * cos_a - cos_b * sin_a;
+    KeyT* row = k + h * p.head_size;
+    const int64_t i1 = p.is_neox ? i : 2 * i;
+    const int64_t i2 = p.is_neox ? i + half : 2 * i + 1;
+    const float x1 = to_f(row[i1]);
+    const float x2 = to_f(row[i2]);
+    row[i1] = from_f<KeyT>(x1 * c - x2 * s);
+    row[i2] = from_f<KeyT>(x2 * c + x1 * s);
+  }
+}
+
+template <typename KeyT, typename CacheT>
+cudaError_t launch_rope_pos(const RopeParams& p, int pos_type, cudaStream_t stream) {
+  const dim3 grid(static_cast<unsigned>(p.num_tokens));
+  if (pos_type == LMCB_DTYPE_INT64) {
+    rope_k_fused_kernel<KeyT, CacheT, int64_t><<<grid, kRopeThreads, 0, stream>>>(p);
+  } else {
+    rope_k_fused_kernel<KeyT, CacheT, int32_t><<<grid, kRopeThreads, 0, stream>>>(p);
+  }
+  return cudaGetLastError();
+}
+
+template <typename KeyT>
+cudaError_t launch_rope_cache(const RopeParams& p, int cache_type, int pos_type,
+                              cudaStream_t stream) {
+  switch (cache_type) {
+    case LMCB_DTYPE_FP32: return launch_rope_pos<KeyT, float>(p, pos_type, stream);
+    case LMCB_DTYPE_BF16: return launch_rope_pos<KeyT, __nv_bfloat16>(p, pos_type, stream);
+    default: return launch_rope_pos<KeyT, __half>(p, pos_type, stream);
+  }
+}
+
+bool float_type(int t) {
+  return t == LMCB_DTYPE_FP32 || t == LMCB_DTYPE_BF16 || t == LMCB_DTYPE_FP16;
+}
+
+}  // namespace
+}  // namespace lmcb
+
+extern "C" {
+
+int lmcb_rotary_embedding_k_fused(const void* oldPositions, const void* newPositions, int posType,
+                                  void* key, int keyType, int64_t numTokens, int64_t numHeads,
+                                  int64_t headSize, int64_t keyTokenStride,
+                                  const void* cosSinCache, int cacheType, int64_t rotDim,
+                                  int64_t maxPosition, int isNeox, void* stream) {
+  lmcb::clear_error();
+  const char* who = "rotary_embedding_k_fused";
+  if (!lmcb::float_type(keyType) || !lmcb::float_type(cacheType)) {
+    return lmcb::fail(LMCB_ERR_UNSUPPORTED_DTYPE, std::string(who) + ": ScalarType not supported.");
+  }
+  if (posType != LMCB_DTYPE_INT64 && posType != LMCB_DTYPE_INT32) {
+    return lmcb::fail(LMCB_ERR_UNSUPPORTED_DTYPE,
+                      std::string(who) + ": positions must be int64 or int32.");
+  }
+  if (numTokens < 0 || numHeads < 0 || headSize <= 0 || rotDim <= 0 || rotDim % 2 != 0 ||
+      rotDim > headSize || maxPosition <= 0 || keyTokenStride < numHeads * headSize ||
+      numTokens > 0x7fffffff) {
+    return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT,
+                      std::string(who) + ": invalid shape (rot_dim must be even and <= head_size).");
+  }
+  if (numTokens == 0 || numHeads == 0) return LMCB_OK;
+  if (oldPositions == nullptr || newPositions == nullptr || key == nullptr ||
+      cosSinCache == nullptr) {
+    return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": NULL pointer.");
+  }
+  lmcb::RopeParams p;
+  p.old_pos = oldPositions;
+  p.new_pos = newPositions;
+  p.key = key;
+  p.cache = cosSinCache;
+  p.num_tokens = numTokens;
+  p.num_heads = numHeads;
+  p.head_size = headSize;
+  p.token_stride = keyTokenStride;
+  p.rot_dim = rotDim;
+  p.max_position = maxPosition;
+  p.is_neox = isNeox ? 1 : 0;
+  p.status = lmcb::device_status_ptr();
+  if (p.status == nullptr) return LMCB_ERR_CUDA;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t err;
+  switch (keyType) {
+    case LMCB_DTYPE_FP32: err = lmcb::launch_rope_cache<float>(p, cacheType, posType, s); break;
+    case LMCB_DTYPE_BF16:
+      err = lmcb::launch_rope_cache<__nv_bfloat16>(p, cacheType, posType, s);
+      break;
+    default: err = lmcb::launch_rope_cache<__half>(p, cacheType, posType, s); break;
+  }
+  if (err != cudaSuccess) return lmcb::cuda_fail(err, who);
+  return LMCB_OK;
+}
+
+}  // extern "C"

@@ -35,6 +35,7 @@ LMCB_DEVICE_FLAG_SLOT_OUT_OF_RANGE = 0x1
 LMCB_DEVICE_FLAG_SYMBOL_OUT_OF_RANGE = 0x2
 LMCB_DEVICE_FLAG_STREAM_OVERFLOW = 0x4
 LMCB_DEVICE_FLAG_WAIT_TIMEOUT = 0x8
+LMCB_DEVICE_FLAG_POSITION_OUT_OF_RANGE = 0x10
 
 LMCB_NOALLOC_STAGING_BYTES = 64 << 20
 
@@ -101,6 +102,11 @@ SIGNATURES: dict[str, tuple] = {
         c_int,
         [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32,
          c_void_p],
+    ),
+    "lmcb_rotary_embedding_k_fused": (
+        c_int,
+        [c_void_p, c_void_p, c_int, c_void_p, c_int, c_int64, c_int64, c_int64, c_int64,
+         c_void_p, c_int, c_int64, c_int64, c_int, c_void_p],
     ),
 }
 

@@ -102,6 +102,17 @@ def test_argument_errors_need_no_gpu():
     assert lib.lmcb_calculate_cdf(8, 8, 1, 4, 4, 257, None) == abi.LMCB_ERR_INVALID_ARGUMENT
     assert lib.lmcb_encode(8, 8, 8, 8, 1, 4, 4, 16, 0, None) == abi.LMCB_ERR_INVALID_ARGUMENT
     assert lib.lmcb_decode_prefsum(8, 8, -1, 8, 8, 1, 4, 4, 16, None) == abi.LMCB_ERR_INVALID_ARGUMENT
+    # rotary: odd rotary width, unsupported dtype
+    assert lib.lmcb_rotary_embedding_k_fused(8, 8, abi.LMCB_DTYPE_INT64, 8, abi.LMCB_DTYPE_BF16,
+                                             4, 2, 64, 128, 8, abi.LMCB_DTYPE_FP32, 63, 100, 1,
+                                             None) == abi.LMCB_ERR_INVALID_ARGUMENT
+    assert lib.lmcb_rotary_embedding_k_fused(8, 8, abi.LMCB_DTYPE_INT64, 8, abi.LMCB_DTYPE_INT32,
+                                             4, 2, 64, 128, 8, abi.LMCB_DTYPE_FP32, 64, 100, 1,
+                                             None) == abi.LMCB_ERR_UNSUPPORTED_DTYPE
+    # batched transfer: negative object count
+    assert lib.lmcb_multi_layer_kv_transfer_batched_kernel(
+        abi.LMCB_DTYPE_BF16, abi.LMCB_DTYPE_INT64, None, 8, 8, 8, 8, -1, 1, 8, 1024, 2, 4, 16,
+        4, 1) == abi.LMCB_ERR_INVALID_ARGUMENT
     # host registry
     assert lib.lmcb_host_register(None, 16, None) == abi.LMCB_ERR_INVALID_ARGUMENT
     assert lib.lmcb_host_get_device_ptr(None) is None
@@ -118,11 +129,13 @@ def test_c_ops_surface_matches_reference():
     assert sys.modules["lmcache.c_ops"] is c_ops
 
 
-def test_c_ops_stubs_raise_not_implemented():
+def test_c_ops_rotary_rejects_cpu_tensors():
+    """The reference's rotary_embedding_k_fused is a stub; here it is
+    implemented for CUDA tensors and rejects anything else."""
     from lmcache_b200 import c_ops
 
     t = torch.zeros(4)
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(RuntimeError, match="CUDA tensors"):
         c_ops.rotary_embedding_k_fused(t, t, t, 4, t, True)
 
 
