@@ -197,6 +197,28 @@ def measure_pcie(dev, stream, nbytes: int = 256 << 20, reps: int = 5) -> dict:
     return out
 
 
+def measure_pcie_concurrent(dev, stream, world: int, nbytes: int = 256 << 20,
+                            reps: int = 3) -> dict:
+    """Whole-job copy-engine bandwidth with every rank copying at once (host
+    barrier, then each rank copies `nbytes` per rep; bytes of all ranks over
+    the slowest rank's time): the host-side ceiling shared by all GPUs."""
+    host = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    devbuf = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    out = {}
+    for name, (dst, src) in (("h2d", (devbuf, host)), ("d2h", (host, devbuf))):
+        torch.cuda.synchronize()
+        barrier(world)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            dst.copy_(src, non_blocking=True)
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms = max_over_ranks(a.elapsed_time(b), world)
+        out[name] = round(world * reps * nbytes / (ms / 1e3) / 1e9, 2)
+    return out
+
+
 def committed_traffic(kernel: str, workload: str):
     """dram read+write bytes per launch from the committed ncu summary, if any."""
     path = os.path.join(ROOT, "profiles", f"{kernel}_{workload}.md")
@@ -413,6 +435,7 @@ def run_ours(args):
     os.environ.pop("LMCB_HOST_RETRIEVE", None)
     best_mode = max(e2e, key=e2e.get)
     pcie = measure_pcie(dev, stream)
+    pcie_all = measure_pcie_concurrent(dev, stream, world)
 
     # ---- CPU baseline (rank 0, N = 1) -----------------------------------
     cpu = None
@@ -477,6 +500,9 @@ def run_ours(args):
                 "by_retrieve_path": {k: round(v, 2) for k, v in e2e.items()},
                 "per_direction_gbs": dir_rates,
                 "pcie_copy_engine_gbs": pcie,
+                "pcie_copy_engine_all_ranks_gbs": pcie_all,
+                "frac_of_all_rank_copy_engines": round(
+                    e2e[best_mode] / ((pcie_all["h2d"] + pcie_all["d2h"]) / 2), 4),
                 # per GPU: the job's e2e rate / ranks, against one GPU's copy engines
                 "frac_of_copy_engine": round(e2e[best_mode] / world /
                                              ((pcie["h2d"] + pcie["d2h"]) / 2), 4),
