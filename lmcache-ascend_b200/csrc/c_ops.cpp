@@ -60,6 +60,18 @@ void* get_kernel_ptr(const torch::Tensor& tensor) {
   return nullptr;
 }
 
+// CUDA tensors of one call must live on the device the kernel runs on: a
+// pointer to another GPU's memory would be dereferenced as a peer access.
+void check_device(const torch::Tensor& t, const torch::Device& dev, const char* name) {
+  TORCH_CHECK(!t.is_cuda() || t.device() == dev, name, " is on ", t.device(),
+              " but the paged KV cache is on ", dev);
+}
+
+torch::Device cuda_device_of(const torch::Device& d) {
+  TORCH_CHECK(d.is_cuda(), "paged_memory_device must be a CUDA device, got ", d);
+  return d.has_index() ? d : torch::Device(torch::kCUDA, c10::cuda::current_device());
+}
+
 void check_status(int status) {
   if (status == LMCB_OK) return;
   if (status == LMCB_ERR_NOT_IMPLEMENTED) {
@@ -159,8 +171,11 @@ void multi_layer_kv_transfer(torch::Tensor& key_value,             // [kv, L, T,
   const int dtype = to_lmcb_dtype(key_value.scalar_type());
   const int slot_dtype = to_slot_dtype(slot_mapping.scalar_type());
 
-  const c10::OptionalDeviceGuard device_guard(paged_memory_device);
-  const c10::OptionalDeviceGuard ptrs_guard(device_of(key_value_ptrs));
+  const torch::Device dev = cuda_device_of(paged_memory_device);
+  check_device(key_value, dev, "key_value");
+  check_device(key_value_ptrs, dev, "key_value_ptrs");
+  check_device(slot_mapping, dev, "slot_mapping");
+  const c10::OptionalDeviceGuard device_guard(dev);
   cudaStream_t stream = current_stream();
 
   const uint64_t* ptrs = static_cast<const uint64_t*>(get_kernel_ptr(key_value_ptrs));
@@ -243,9 +258,12 @@ void multi_layer_kv_transfer_batched(const std::vector<torch::Tensor>& key_value
   if (total == 0) return;
   TORCH_CHECK(total < (int64_t(1) << 31), "too many tokens in one batch");
 
-  const c10::OptionalDeviceGuard device_guard(paged_memory_device);
+  const torch::Device dev = cuda_device_of(paged_memory_device);
+  check_device(key_value_ptrs, dev, "key_value_ptrs");
+  check_device(slot_mapping, dev, "slot_mapping");
+  for (const auto& t : key_values) check_device(t, dev, "key_values");
+  const c10::OptionalDeviceGuard device_guard(dev);
   cudaStream_t stream = current_stream();
-  const auto dev = torch::Device(torch::kCUDA, c10::cuda::current_device());
   const uint64_t* ptrs = static_cast<const uint64_t*>(get_kernel_ptr(key_value_ptrs));
   const void* slots = get_kernel_ptr(slot_mapping);
   const int64_t esz = first.element_size();
@@ -326,7 +344,12 @@ void multi_layer_kv_transfer_unilateral(torch::Tensor& key_value,
               "key_value is smaller than [2, ", num_layers, ", ", num_tokens, ", ", hidden, "]");
   const int dtype = to_lmcb_dtype(key_value.scalar_type());
   const int slot_dtype = to_slot_dtype(slot_mapping.scalar_type());
-  const c10::OptionalDeviceGuard device_guard(paged_memory_device);
+  const torch::Device dev = cuda_device_of(paged_memory_device);
+  check_device(key_value, dev, "key_value");
+  check_device(key_ptrs, dev, "key_ptrs");
+  check_device(value_ptrs, dev, "value_ptrs");
+  check_device(slot_mapping, dev, "slot_mapping");
+  const c10::OptionalDeviceGuard device_guard(dev);
   cudaStream_t stream = current_stream();
   check_status(lmcb_multi_layer_kv_transfer_unilateral_kernel(
       dtype, slot_dtype, stream, static_cast<const uint64_t*>(get_kernel_ptr(key_ptrs)),
@@ -356,8 +379,12 @@ void single_layer_kv_transfer(torch::Tensor& lmc_key_value_cache,  // [T,2,H] or
   const int dtype = to_lmcb_dtype(vllm_key_cache.scalar_type());
   const int slot_dtype = to_slot_dtype(slot_mapping.scalar_type());
 
-  const c10::OptionalDeviceGuard device_guard(device_of(vllm_key_cache));
-  const c10::OptionalDeviceGuard slot_device_guard(device_of(slot_mapping));
+  TORCH_CHECK(vllm_key_cache.is_cuda(), "vllm_key_cache must be a CUDA tensor");
+  const torch::Device dev = vllm_key_cache.device();
+  check_device(vllm_value_cache, dev, "vllm_value_cache");
+  check_device(lmc_key_value_cache, dev, "lmc_key_value_cache");
+  check_device(slot_mapping, dev, "slot_mapping");
+  const c10::OptionalDeviceGuard device_guard(dev);
   cudaStream_t stream = current_stream();
   check_status(lmcb_single_layer_kv_transfer_kernel(
       dtype, slot_dtype, stream, get_kernel_ptr(lmc_key_value_cache),
@@ -389,7 +416,12 @@ void flash_transfer(torch::Tensor& key_value, torch::Tensor& key_cache,
               "K and V caches must have the same number of blocks and block size");
   const int dtype = to_lmcb_dtype(key_value.scalar_type());
   const int slot_dtype = to_slot_dtype(slot_mapping.scalar_type());
-  const c10::OptionalDeviceGuard device_guard(device_of(key_cache));
+  TORCH_CHECK(key_cache.is_cuda(), "key_cache must be a CUDA tensor");
+  const torch::Device dev = key_cache.device();
+  check_device(value_cache, dev, "value_cache");
+  check_device(key_value, dev, "key_value");
+  check_device(slot_mapping, dev, "slot_mapping");
+  const c10::OptionalDeviceGuard device_guard(dev);
   cudaStream_t stream = current_stream();
   check_status(lmcb_load_and_reshape_flash_kernel(
       dtype, slot_dtype, stream, get_kernel_ptr(key_value), get_kernel_ptr(key_cache),

@@ -156,6 +156,12 @@ def test_c_ops_errors_match_reference_messages():
                                       torch.zeros(1, dtype=torch.int64),
                                       torch.zeros(4, dtype=torch.float32), torch.device("cpu"), 16,
                                       True, False)
+    # the paged cache must be on a CUDA device
+    with pytest.raises(RuntimeError, match="must be a CUDA device"):
+        c_ops.multi_layer_kv_transfer(torch.zeros(2, 1, 4, 8, dtype=torch.bfloat16),
+                                      torch.zeros(1, dtype=torch.int64),
+                                      torch.zeros(4, dtype=torch.int64), torch.device("cpu"), 16,
+                                      True, False)
     # shape checks come before any device work
     with pytest.raises(RuntimeError, match="smaller than"):
         c_ops.multi_layer_kv_transfer(torch.zeros(2, 1, 2, 8, dtype=torch.bfloat16),
