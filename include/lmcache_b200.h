@@ -192,6 +192,24 @@ LMCB_API int lmcb_multi_layer_kv_retrieve_staged(int type, int slotType, void* s
                                         int32_t numLayers, int64_t pageBuffSize,
                                         int32_t numTokensChunk);
 
+/* Store (paged -> LMCache) into a pinned host LMCache object through a
+ * caller-provided device staging buffer and one device-to-host DMA, instead of
+ * zero-copy kernel writes. Same result as lmcb_multi_layer_kv_transfer_kernel
+ * with page2L != 0: a row whose slot is skipped is first read from the host
+ * object (through hostCacheDevice, its device-mapped alias) into the staging
+ * buffer, so the copy back leaves it unchanged.
+ *   hostCacheTensor  host address of the object (DMA destination)
+ *   hostCacheDevice  device-mapped alias of the same object (lmcb_host_register)
+ *   staging          device scratch of stagingBytes >= the object's size */
+LMCB_API int lmcb_multi_layer_kv_store_staged(int type, int slotType, void* stream,
+                                              const uint64_t* pagedKVCaches,
+                                              void* hostCacheTensor,
+                                              const void* hostCacheDevice, void* staging,
+                                              size_t stagingBytes, const void* slotmappings,
+                                              int64_t hiddenDims, int32_t kvs,
+                                              int32_t numLayers, int64_t pageBuffSize,
+                                              int32_t numTokensChunk);
+
 /* Size of the staging area that lmcb_multi_layer_kv_retrieve_staged_noalloc
  * keeps on every GPU where the library is loaded (64 MiB). */
 #define LMCB_NOALLOC_STAGING_BYTES (64u << 20)

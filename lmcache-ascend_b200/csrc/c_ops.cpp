@@ -107,13 +107,16 @@ int64_t paged_row_stride(const torch::Tensor& cache, int64_t hidden, const char*
 
 enum class HostRetrievePath { kAuto, kZeroCopy, kDma };
 
-HostRetrievePath host_retrieve_path() {
-  const char* env = std::getenv("LMCB_HOST_RETRIEVE");
+HostRetrievePath host_path_from_env(const char* name) {
+  const char* env = std::getenv(name);
   if (env == nullptr) return HostRetrievePath::kAuto;
   if (std::strcmp(env, "zerocopy") == 0) return HostRetrievePath::kZeroCopy;
   if (std::strcmp(env, "dma") == 0) return HostRetrievePath::kDma;
   return HostRetrievePath::kAuto;
 }
+
+HostRetrievePath host_retrieve_path() { return host_path_from_env("LMCB_HOST_RETRIEVE"); }
+HostRetrievePath host_store_path() { return host_path_from_env("LMCB_HOST_STORE"); }
 
 // Objects at least this large are retrieved from pinned host memory with one
 // DMA into a device staging buffer plus an HBM scatter instead of zero-copy
@@ -121,6 +124,11 @@ HostRetrievePath host_retrieve_path() {
 //   2 MiB: zero-copy 46.6 GB/s, DMA 39.5;   8 MiB: 50.1 vs 50.7;
 //   32 MiB: 51.1 vs 53.6;                    64 MiB: 51.3 vs 54.0.
 constexpr int64_t kDmaRetrieveMinBytes = int64_t(8) << 20;
+
+// Same choice for stores into pinned host memory: gather into a device
+// staging buffer (skipped rows read back from the object) and one DMA to the
+// host, instead of zero-copy kernel writes.
+constexpr int64_t kDmaStoreMinBytes = int64_t(8) << 20;
 
 }  // namespace
 
@@ -200,6 +208,23 @@ void multi_layer_kv_transfer(torch::Tensor& key_value,             // [kv, L, T,
           static_cast<size_t>(bytes), slots, hidden, kv_size,
           static_cast<int32_t>(num_layers), page_buffer_size,
           static_cast<int32_t>(num_tokens)));
+      return;
+    }
+  }
+  if (key_value.device().is_cpu() && direction) {
+    const int64_t bytes = kv_size * num_layers * num_tokens * hidden * key_value.element_size();
+    const HostRetrievePath path = host_store_path();
+    const bool use_dma = path == HostRetrievePath::kDma ||
+                         (path == HostRetrievePath::kAuto && bytes >= kDmaStoreMinBytes);
+    if (use_dma && bytes > 0) {
+      void* host_dev = get_kernel_ptr(key_value);  // registered: device alias
+      auto staging = torch::empty(
+          {bytes}, torch::TensorOptions().dtype(torch::kUInt8).device(
+                       torch::kCUDA, c10::cuda::current_device()));
+      check_status(lmcb_multi_layer_kv_store_staged(
+          dtype, slot_dtype, stream, ptrs, key_value.data_ptr(), host_dev, staging.data_ptr(),
+          static_cast<size_t>(bytes), slots, hidden, kv_size, static_cast<int32_t>(num_layers),
+          page_buffer_size, static_cast<int32_t>(num_tokens)));
       return;
     }
   }

@@ -76,6 +76,10 @@ struct TransferParams {
   FastDiv row_vecs;        // row_bytes / VEC
   int32_t page2L;          // 1: paged -> LMCache, 0: LMCache -> paged
   unsigned int* status;
+  // Vector kernel, single object, page2L only: device-mapped alias of the
+  // final destination object (same layout as lmc); rows with a skipped slot
+  // are copied from it instead of being left untouched. Null otherwise.
+  const uint8_t* fallback;
   // kBatched only. Tokens t are numbered across all objects: object i holds
   // t in [obj_offsets[i], obj_offsets[i+1]) (num_objects + 1 prefix sums),
   // laid out [kv, num_layers, T_i, hidden] at obj_ptrs[i], and takes its slot
@@ -182,6 +186,14 @@ transfer_rows_kernel(const TransferParams p) {
           src = lmc;
           dst = paged;
         }
+        misaligned = ((reinterpret_cast<uintptr_t>(src) |
+                       reinterpret_cast<uintptr_t>(dst)) & (VEC - 1)) != 0;
+      } else if (p.fallback != nullptr && p.page2L) {
+        // Staged store: a skipped row of the staging copy takes the row the
+        // destination object already holds, so the copy back leaves it as is.
+        src = p.fallback + (lmc - p.lmc);
+        dst = lmc;
+        valid = true;
         misaligned = ((reinterpret_cast<uintptr_t>(src) |
                        reinterpret_cast<uintptr_t>(dst)) & (VEC - 1)) != 0;
       }
@@ -670,7 +682,8 @@ cudaError_t launch_slot(const TransferParams& p, int vec, int mode, int grid,
 // must all be multiples of the vector width.
 int launch_transfer(TransferParams p, int type, int slot_type, int mode,
                     std::initializer_list<uint64_t> alignment_terms,
-                    cudaStream_t stream, const char* who, bool objects_on_device = false) {
+                    cudaStream_t stream, const char* who, bool objects_on_device = false,
+                    bool force_vector = false) {
   const int esz = dtype_size(type);
   if (esz == 0) {
     return fail(LMCB_ERR_UNSUPPORTED_DTYPE, std::string(who) + ": ScalarType not supported.");
@@ -719,7 +732,7 @@ int launch_transfer(TransferParams p, int type, int slot_type, int mode,
   const bool bulk_ok = vec == 16 && p.row_bytes % 16 == 0 && p.row_bytes <= stage_bytes &&
                        lmc_on_device;
   const int64_t total_rows = static_cast<int64_t>(p.num_kv) * p.num_layers * p.num_tokens;
-  if (bulk_ok && forced != 1 && total_rows < (int64_t(1) << 31)) {
+  if (bulk_ok && forced != 1 && !force_vector && total_rows < (int64_t(1) << 31)) {
     BulkParams b;
     b.num_rows = static_cast<int32_t>(total_rows);
     int64_t rows = stage_bytes / p.row_bytes;
@@ -969,6 +982,66 @@ int lmcb_multi_layer_kv_transfer_batched_kernel(
   return lmcb::launch_transfer(p, type, slotType, lmcb::kBatched,
                                {static_cast<uint64_t>(row), static_cast<uint64_t>(p.page_kv_offset)},
                                static_cast<cudaStream_t>(stream), who, objectsOnDevice != 0);
+}
+
+int lmcb_multi_layer_kv_store_staged(int type, int slotType, void* stream,
+                                     const uint64_t* pagedKVCaches, void* hostCacheTensor,
+                                     const void* hostCacheDevice, void* staging,
+                                     size_t stagingBytes, const void* slotmappings,
+                                     int64_t hiddenDims, int32_t kvs, int32_t numLayers,
+                                     int64_t pageBuffSize, int32_t numTokensChunk) {
+  lmcb::clear_error();
+  const char* who = "multi_layer_kv_store_staged";
+  const int64_t esz = lmcb::dtype_size(type);
+  if (esz == 0) {
+    return lmcb::fail(LMCB_ERR_UNSUPPORTED_DTYPE, std::string(who) + ": ScalarType not supported.");
+  }
+  if (kvs != 1 && kvs != 2) {
+    return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": kvs must be 1 or 2.");
+  }
+  if (kvs == 2 && pageBuffSize <= 0) {
+    return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT,
+                      std::string(who) + ": page_buffer_size must be positive for K/V caches.");
+  }
+  if (numTokensChunk <= 0 || numLayers <= 0) return LMCB_OK;
+  const int64_t row = hiddenDims * esz;
+  const size_t bytes = static_cast<size_t>(kvs) * numLayers * numTokensChunk * row;
+  if (hostCacheTensor == nullptr || hostCacheDevice == nullptr || staging == nullptr) {
+    return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": NULL pointer.");
+  }
+  if (stagingBytes < bytes) {
+    return lmcb::fail(LMCB_ERR_CAPACITY,
+                      std::string(who) + ": staging buffer holds " + std::to_string(stagingBytes) +
+                          " bytes, the object needs " + std::to_string(bytes));
+  }
+  TransferParams p{};
+  p.lmc = static_cast<uint8_t*>(staging);
+  p.lmc_token_stride = row;
+  p.lmc_layer_stride = row * numTokensChunk;
+  p.lmc_kv_stride = p.lmc_layer_stride * numLayers;
+  p.ptrs_k = pagedKVCaches;
+  p.ptrs_v = pagedKVCaches;
+  p.page_kv_offset = pageBuffSize * row;
+  p.paged_row_stride = row;
+  p.num_paged_rows = pageBuffSize;
+  p.slots = slotmappings;
+  p.num_tokens = numTokensChunk;
+  p.num_layers = numLayers;
+  p.num_kv = kvs;
+  p.row_bytes = row;
+  p.page2L = 1;
+  p.fallback = static_cast<const uint8_t*>(hostCacheDevice);
+  // The gather reads skipped rows from host memory, so it runs on the
+  // vectorised kernel (the bulk-copy path only addresses device memory).
+  const int rc = lmcb::launch_transfer(
+      p, type, slotType, lmcb::kPtrArray,
+      {reinterpret_cast<uint64_t>(staging), static_cast<uint64_t>(row),
+       static_cast<uint64_t>(p.page_kv_offset), reinterpret_cast<uint64_t>(hostCacheDevice)},
+      static_cast<cudaStream_t>(stream), who, false, /*force_vector=*/true);
+  if (rc != LMCB_OK) return rc;
+  LMCB_CUDA_TRY(cudaMemcpyAsync(hostCacheTensor, staging, bytes, cudaMemcpyDeviceToHost,
+                                static_cast<cudaStream_t>(stream)));
+  return LMCB_OK;
 }
 
 int lmcb_multi_layer_kv_retrieve_staged(int type, int slotType, void* stream,

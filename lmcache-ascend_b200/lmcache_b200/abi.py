@@ -75,6 +75,11 @@ SIGNATURES: dict[str, tuple] = {
         [c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_int64,
          c_int32, c_int32, c_int64, c_int32],
     ),
+    "lmcb_multi_layer_kv_store_staged": (
+        c_int,
+        [c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p,
+         c_int64, c_int32, c_int32, c_int64, c_int32],
+    ),
     "lmcb_multi_layer_kv_retrieve_staged_noalloc": (
         c_int,
         [c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int32, c_int32,

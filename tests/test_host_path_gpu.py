@@ -87,6 +87,32 @@ def test_pinned_retrieve_paths(mode, name, monkeypatch):
     arena.close()
 
 
+@pytest.mark.parametrize("mode", ["zerocopy", "dma"])
+@pytest.mark.parametrize("name", ["c1", "c4", "c5"])
+def test_pinned_store_paths(mode, name, monkeypatch):
+    """Store into a pinned-host object through both host paths. The staged
+    path gathers into a device buffer and copies it back with one DMA; rows
+    of skipped slots must still keep the object's previous contents."""
+    monkeypatch.setenv("LMCB_HOST_STORE", mode)
+    spec = wl.SPECS[name]
+    kv = wl.make_kv_caches(spec, DEV, seed=6)
+    slots = wl.make_slot_mapping(spec, seed=6)
+    sc = wl.chunks(slots, spec.chunk_size)[0].clone()
+    sc[7] = -1
+    sc[200] = -1
+    arena = PinMemoryAllocator(64 << 20)
+    obj = arena.allocate(spec.memobj_shape(len(sc)), torch.bfloat16).tensor
+    obj.copy_(torch.randn(obj.shape).to(torch.bfloat16))  # previous contents
+    want = bits(obj).copy()
+    c_ops.multi_layer_kv_transfer(obj, wl.pointer_tensor(kv, DEV), sc.to(DEV), kv[0].device,
+                                  spec.page_buffer_size, True, spec.use_mla)
+    torch.cuda.synchronize()
+    oracle.multi_layer_kv_transfer(want, [bits(t) for t in kv], sc.numpy(),
+                                   spec.page_buffer_size, True, spec.use_mla)
+    assert np.array_equal(bits(obj), want)
+    arena.close()
+
+
 def test_staged_retrieve_through_abi_and_capacity_error():
     spec = wl.SPECS["c1"]
     kv = wl.make_kv_caches(spec, DEV, seed=4)
