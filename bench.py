@@ -203,36 +203,39 @@ def measure_pcie(dev, stream, nbytes: int = 256 << 20, reps: int = 5) -> dict:
     return out
 
 
-def measure_pcie_duplex(dev, world: int, nbytes: int = 256 << 20, reps: int = 3) -> float:
+def measure_pcie_duplex(dev, world: int, chunk: int = 32 << 20, n: int = 32) -> float:
     """Whole-job copy-engine bandwidth with both directions at once: on every
-    rank an H2D stream and a D2H stream each copy `nbytes` `reps` times
+    rank an H2D stream and a D2H stream each copy `n` chunks of `chunk` bytes
     (bytes of all ranks and both directions over the slowest rank's time).
     The ceiling of the two-stream pinned-host step."""
-    h_src = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
-    h_dst = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
-    d_src = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-    d_dst = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    h_src = torch.empty(chunk * 4, dtype=torch.uint8).pin_memory()
+    h_dst = torch.empty(chunk * 4, dtype=torch.uint8).pin_memory()
+    d_src = torch.empty(chunk * 4, dtype=torch.uint8, device=dev)
+    d_dst = torch.empty(chunk * 4, dtype=torch.uint8, device=dev)
     up, down = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
-    torch.cuda.synchronize()
-    barrier(world)
-    a = torch.cuda.Event(enable_timing=True)
-    a.record(torch.cuda.current_stream())
-    up.wait_event(a)
-    down.wait_event(a)
-    with torch.cuda.stream(up):
-        for _ in range(reps):
-            d_dst.copy_(h_src, non_blocking=True)
-    with torch.cuda.stream(down):
-        for _ in range(reps):
-            h_dst.copy_(d_src, non_blocking=True)
-    cur = torch.cuda.current_stream()
-    cur.wait_stream(up)
-    cur.wait_stream(down)
-    b = torch.cuda.Event(enable_timing=True)
-    b.record(cur)
-    torch.cuda.synchronize()
-    ms = max_over_ranks(a.elapsed_time(b), world)
-    return round(world * 2 * reps * nbytes / (ms / 1e3) / 1e9, 2)
+    best = 0.0
+    for _ in range(3):
+        torch.cuda.synchronize()
+        barrier(world)
+        cur = torch.cuda.current_stream()
+        a = torch.cuda.Event(enable_timing=True)
+        a.record(cur)
+        up.wait_event(a)
+        down.wait_event(a)
+        for i in range(n):
+            j = (i % 4) * chunk
+            with torch.cuda.stream(up):
+                d_dst[j:j + chunk].copy_(h_src[j:j + chunk], non_blocking=True)
+            with torch.cuda.stream(down):
+                h_dst[j:j + chunk].copy_(d_src[j:j + chunk], non_blocking=True)
+        cur.wait_stream(up)
+        cur.wait_stream(down)
+        b = torch.cuda.Event(enable_timing=True)
+        b.record(cur)
+        torch.cuda.synchronize()
+        ms = max_over_ranks(a.elapsed_time(b), world)
+        best = max(best, world * 2 * n * chunk / (ms / 1e3) / 1e9)
+    return round(best, 2)
 
 
 def measure_pcie_concurrent(dev, stream, world: int, nbytes: int = 256 << 20,
