@@ -1,6 +1,6 @@
 /*
  * cachegen_ref.c -- CPU oracle of the CacheGen codec entry points (test
- * infrastructure only: the tests and the smoke check call it as the checker).
+ * infrastructure only: the tests and the smoke check compare the kernels with it).
  *
  * Reference status: LMCache-Ascend exports calculate_cdf, encode_fast_new,
  * decode_fast_new and decode_fast_prefsum (csrc/pybind.cpp:21-24) but every

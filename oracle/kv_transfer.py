@@ -1,6 +1,6 @@
 """CPU oracle of LMCache-Ascend's paged KV-cache transfer ops (test infrastructure).
 
-This module is the checker, not the product: only the tests, the smoke check
+This module is test infrastructure, not the product: only the tests, the smoke check
 and the CPU-baseline leg of the benchmark may import it. Nothing on the
 product path calls into it.
 
