@@ -143,6 +143,21 @@ LMCB_API int lmcb_multi_layer_kv_transfer_batched_kernel(
     int32_t numObjects, int objectsOnDevice, const void* slotmappings, int64_t hiddenDims,
     int32_t kvs, int32_t numLayers, int64_t pageBuffSize, int32_t totalTokens, int page2L);
 
+/* single_layer_kv_transfer for many objects in one launch (the layerwise
+ * connector moves every chunk of a request for one layer this way, where the
+ * reference issues one call per chunk, npu_connector.py:227-252). Object i
+ * (at objectPtrs[i]) holds T_i = tokenOffsets[i+1] - tokenOffsets[i] tokens
+ * with slot ids slotmappings[slotStarts[i] ... + T_i), laid out [T_i, 2,
+ * hiddenDims] if tokenMajor else [2, T_i, hiddenDims]. Caches, strides and
+ * bounds as in lmcb_single_layer_kv_transfer_kernel; objectsOnDevice as in
+ * lmcb_multi_layer_kv_transfer_batched_kernel. */
+LMCB_API int lmcb_single_layer_kv_transfer_batched_kernel(
+    int type, int slotType, void* stream, const uint64_t* objectPtrs,
+    const int64_t* tokenOffsets, const int64_t* slotStarts, int32_t numObjects,
+    int objectsOnDevice, void* keyCachePtr, void* valueCachePtr, const void* slotmappings,
+    int64_t hiddenDims, int32_t totalTokens, int page2L, int tokenMajor,
+    int64_t pagedRowStride, int64_t numPagedRows);
+
 /* One layer, separate K and V caches.
  * Replaces kvcache_ops::single_layer_kv_transfer_kernel (csrc/mem_kernels.h:14-18),
  * launched by single_layer_kv_transfer (csrc/mem_kernels.cpp:108-152).

@@ -348,6 +348,76 @@ void multi_layer_kv_transfer_batched(const std::vector<torch::Tensor>& key_value
       direction ? 1 : 0));
 }
 
+// single_layer_kv_transfer for every chunk of a layer in one launch (an
+// addition to the reference surface, used by the layerwise connector).
+// lmc_kvs[i] is [T_i, 2, H] (token_major) or [2, T_i, H] and holds
+// slot_mapping[starts[i]:ends[i]]; all CUDA tensors on the caches' device, or
+// all registered pinned host tensors (zero-copy).
+void single_layer_kv_transfer_batched(const std::vector<torch::Tensor>& lmc_kvs,
+                                      torch::Tensor& vllm_key_cache,
+                                      torch::Tensor& vllm_value_cache,
+                                      torch::Tensor& slot_mapping,
+                                      const std::vector<int64_t>& starts,
+                                      const std::vector<int64_t>& ends, const bool direction,
+                                      const bool token_major) {
+  const int64_t n = static_cast<int64_t>(lmc_kvs.size());
+  TORCH_CHECK(static_cast<int64_t>(starts.size()) == n && static_cast<int64_t>(ends.size()) == n,
+              "starts and ends must have one entry per object");
+  if (n == 0) return;
+  TORCH_CHECK(vllm_key_cache.is_cuda(), "vllm_key_cache must be a CUDA tensor");
+  const torch::Device dev = vllm_key_cache.device();
+  check_device(vllm_value_cache, dev, "vllm_value_cache");
+  check_device(slot_mapping, dev, "slot_mapping");
+  const int64_t hidden = lmc_kvs[0].size(-1);
+  const bool on_device = lmc_kvs[0].is_cuda();
+  TORCH_CHECK(vllm_key_cache.scalar_type() == lmc_kvs[0].scalar_type() &&
+                  vllm_value_cache.scalar_type() == lmc_kvs[0].scalar_type(),
+              "K/V caches and the objects must have the same dtype");
+  const int64_t k_stride = paged_row_stride(vllm_key_cache, hidden, "vllm_key_cache");
+  const int64_t v_stride = paged_row_stride(vllm_value_cache, hidden, "vllm_value_cache");
+  TORCH_CHECK(k_stride == v_stride, "K and V caches must have the same row stride");
+  const int64_t rows = std::min(vllm_key_cache.size(0) * vllm_key_cache.size(1),
+                                vllm_value_cache.size(0) * vllm_value_cache.size(1));
+  int64_t total = 0;
+  for (int64_t i = 0; i < n; ++i) {
+    const auto& t = lmc_kvs[i];
+    check_device(t, dev, "lmc_kvs");
+    TORCH_CHECK(t.scalar_type() == lmc_kvs[0].scalar_type() && t.size(-1) == hidden &&
+                    t.is_cuda() == on_device && t.is_contiguous(),
+                "objects must share dtype, hidden size and residency, and be contiguous");
+    TORCH_CHECK(0 <= starts[i] && starts[i] <= ends[i] && ends[i] <= slot_mapping.size(0),
+                "object ", i, ": slot range out of bounds");
+    TORCH_CHECK(t.numel() >= 2 * (ends[i] - starts[i]) * hidden, "object ", i,
+                " is smaller than its slot range");
+    total += ends[i] - starts[i];
+  }
+  if (total == 0) return;
+  TORCH_CHECK(total < (int64_t(1) << 31), "too many tokens in one batch");
+  const int dtype = to_lmcb_dtype(vllm_key_cache.scalar_type());
+  const int slot_dtype = to_slot_dtype(slot_mapping.scalar_type());
+  const c10::OptionalDeviceGuard device_guard(dev);
+  cudaStream_t stream = current_stream();
+  auto table = torch::empty({3 * n + 1},
+                            torch::TensorOptions().dtype(torch::kLong).pinned_memory(true));
+  int64_t* tab = table.data_ptr<int64_t>();
+  int64_t off = 0;
+  for (int64_t i = 0; i < n; ++i) {
+    const int64_t count = ends[i] - starts[i];
+    tab[i] = count == 0 ? 0 : reinterpret_cast<int64_t>(get_kernel_ptr(lmc_kvs[i]));
+    tab[n + i] = off;
+    tab[2 * n + 1 + i] = starts[i];
+    off += count;
+  }
+  tab[2 * n] = off;
+  auto table_dev = table.to(dev, /*non_blocking=*/true);
+  const int64_t* td = table_dev.data_ptr<int64_t>();
+  check_status(lmcb_single_layer_kv_transfer_batched_kernel(
+      dtype, slot_dtype, stream, reinterpret_cast<const uint64_t*>(td), td + n, td + 2 * n + 1,
+      static_cast<int32_t>(n), on_device ? 1 : 0, get_kernel_ptr(vllm_key_cache),
+      get_kernel_ptr(vllm_value_cache), get_kernel_ptr(slot_mapping), hidden,
+      static_cast<int32_t>(total), direction ? 1 : 0, token_major ? 1 : 0, k_stride, rows));
+}
+
 void multi_layer_kv_transfer_unilateral(torch::Tensor& key_value,
                                         const torch::Tensor& key_ptrs,
                                         const torch::Tensor& value_ptrs,
@@ -631,6 +701,7 @@ PYBIND11_MODULE(c_ops, m) {
   m.def("rotary_embedding_k_fused", &rotary_embedding_k_fused);
   // Additions beyond the reference surface.
   m.def("multi_layer_kv_transfer_batched", &multi_layer_kv_transfer_batched);
+  m.def("single_layer_kv_transfer_batched", &single_layer_kv_transfer_batched);
   m.def("host_unregister", &unregister_memory);
   m.def("get_device_ptr", &get_device_ptr);
   m.def("device_status", &device_status);

@@ -47,7 +47,15 @@ constexpr int kTargetTileBytes = 32 * 1024;
 //   kDirect:   paged base = base_k (kv == 0) or base_v (kv == 1); one object.
 //   kBatched:  paged side as kPtrArray; many LMCache objects, located through
 //              the object table (see TransferParams::obj_*).
-enum PagedMode { kPtrArray = 0, kDirect = 1, kBatched = 2 };
+//   kBatchedDirect: paged side as kDirect (one layer); many objects.
+enum PagedMode { kPtrArray = 0, kDirect = 1, kBatched = 2, kBatchedDirect = 3 };
+
+__host__ __device__ constexpr bool paged_direct(int mode) {
+  return mode == kDirect || mode == kBatchedDirect;
+}
+__host__ __device__ constexpr bool batched_mode(int mode) {
+  return mode == kBatched || mode == kBatchedDirect;
+}
 
 struct TransferParams {
   // LMCache side: row(kv, layer, t) = lmc + kv*lmc_kv_stride
@@ -88,13 +96,16 @@ struct TransferParams {
   const int64_t* obj_offsets;
   const int64_t* obj_slot_starts;
   int32_t num_objects;
+  // Object layout: 0 = [kv, num_layers, T_i, hidden];
+  //                1 = token-major [T_i, kv, hidden] (single layer).
+  int32_t obj_token_major;
 };
 
 // LMCache-side row address of (kv, layer, t) and the index of t's slot id.
 template <int MODE>
 __device__ __forceinline__ uint8_t* lmc_row(const TransferParams& p, int kv, int layer, int t,
                                             int64_t* slot_index) {
-  if (MODE == kBatched) {
+  if (batched_mode(MODE)) {
     // Last object whose first token is <= t (empty objects are skipped over).
     int lo = 0, hi = p.num_objects;  // obj_offsets[lo] <= t < obj_offsets[hi]
     while (hi - lo > 1) {
@@ -105,8 +116,10 @@ __device__ __forceinline__ uint8_t* lmc_row(const TransferParams& p, int kv, int
     const int64_t count = __ldg(p.obj_offsets + lo + 1) - first;
     const int64_t j = t - first;
     *slot_index = __ldg(p.obj_slot_starts + lo) + j;
-    return reinterpret_cast<uint8_t*>(__ldg(p.obj_ptrs + lo)) +
-           ((static_cast<int64_t>(kv) * p.num_layers + layer) * count + j) * p.row_bytes;
+    const int64_t row = p.obj_token_major
+                            ? j * p.num_kv + kv
+                            : (static_cast<int64_t>(kv) * p.num_layers + layer) * count + j;
+    return reinterpret_cast<uint8_t*>(__ldg(p.obj_ptrs + lo)) + row * p.row_bytes;
   }
   *slot_index = t;
   return p.lmc + kv * p.lmc_kv_stride + layer * p.lmc_layer_stride +
@@ -172,7 +185,7 @@ transfer_rows_kernel(const TransferParams p) {
       }
       if (valid) {
         uint8_t* paged;
-        if (MODE != kDirect) {
+        if (!paged_direct(MODE)) {
           const uint64_t* arr = kv == 0 ? p.ptrs_k : p.ptrs_v;
           paged = reinterpret_cast<uint8_t*>(arr[layer]) + kv * p.page_kv_offset;
         } else {
@@ -400,7 +413,7 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b) {
         int64_t slot_index;
         lmcs[j] = lmc_row<MODE>(p, kv, layer, tok, &slot_index);
         slot[j] = static_cast<int64_t>(slots[slot_index]);
-        if (MODE != kDirect) {
+        if (!paged_direct(MODE)) {
           const uint64_t* arr = kv == 0 ? p.ptrs_k : p.ptrs_v;
           base[j] = reinterpret_cast<uint8_t*>(arr[layer]) + kv * p.page_kv_offset;
         } else {
@@ -623,7 +636,8 @@ cudaError_t launch_bulk(const TransferParams& p, const BulkParams& b, int mode, 
   switch (mode) {
     case kPtrArray: return launch_bulk_mode<SlotT, kPtrArray>(p, b, grid, stream);
     case kDirect: return launch_bulk_mode<SlotT, kDirect>(p, b, grid, stream);
-    default: return launch_bulk_mode<SlotT, kBatched>(p, b, grid, stream);
+    case kBatched: return launch_bulk_mode<SlotT, kBatched>(p, b, grid, stream);
+    default: return launch_bulk_mode<SlotT, kBatchedDirect>(p, b, grid, stream);
   }
 }
 
@@ -660,9 +674,12 @@ cudaError_t launch_vec(const TransferParams& p, int mode, int grid, cudaStream_t
     case kDirect:
       return launch_ex(&transfer_rows_kernel<SlotT, VEC, kDirect>, dim3(grid), dim3(kThreads), 0,
                        stream, p);
-    default:
+    case kBatched:
       return launch_ex(&transfer_rows_kernel<SlotT, VEC, kBatched>, dim3(grid), dim3(kThreads),
                        0, stream, p);
+    default:
+      return launch_ex(&transfer_rows_kernel<SlotT, VEC, kBatchedDirect>, dim3(grid),
+                       dim3(kThreads), 0, stream, p);
   }
 }
 
@@ -696,18 +713,18 @@ int launch_transfer(TransferParams p, int type, int slot_type, int mode,
     return fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": negative size.");
   }
   if (p.num_tokens == 0 || p.num_layers == 0) return LMCB_OK;
-  if ((mode != kBatched && p.lmc == nullptr) || p.slots == nullptr) {
+  if ((!batched_mode(mode) && p.lmc == nullptr) || p.slots == nullptr) {
     return fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": NULL pointer.");
   }
-  if (mode == kBatched &&
+  if (batched_mode(mode) &&
       (p.obj_ptrs == nullptr || p.obj_offsets == nullptr || p.obj_slot_starts == nullptr ||
        p.num_objects <= 0)) {
     return fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": NULL object table.");
   }
-  if (mode != kDirect && (p.ptrs_k == nullptr || p.ptrs_v == nullptr)) {
+  if (!paged_direct(mode) && (p.ptrs_k == nullptr || p.ptrs_v == nullptr)) {
     return fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": NULL pointer array.");
   }
-  if (mode == kDirect && (p.base_k == nullptr || (p.num_kv > 1 && p.base_v == nullptr))) {
+  if (paged_direct(mode) && (p.base_k == nullptr || (p.num_kv > 1 && p.base_v == nullptr))) {
     return fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": NULL cache pointer.");
   }
   p.status = device_status_ptr();
@@ -728,7 +745,7 @@ int launch_transfer(TransferParams p, int type, int slot_type, int mode,
   }();
   const BulkConfig bc = bulk_config();
   const int64_t stage_bytes = static_cast<int64_t>(bc.stage_kb) * 1024;
-  const bool lmc_on_device = mode == kBatched ? objects_on_device : is_device_memory(p.lmc);
+  const bool lmc_on_device = batched_mode(mode) ? objects_on_device : is_device_memory(p.lmc);
   const bool bulk_ok = vec == 16 && p.row_bytes % 16 == 0 && p.row_bytes <= stage_bytes &&
                        lmc_on_device;
   const int64_t total_rows = static_cast<int64_t>(p.num_kv) * p.num_layers * p.num_tokens;
@@ -982,6 +999,43 @@ int lmcb_multi_layer_kv_transfer_batched_kernel(
   return lmcb::launch_transfer(p, type, slotType, lmcb::kBatched,
                                {static_cast<uint64_t>(row), static_cast<uint64_t>(p.page_kv_offset)},
                                static_cast<cudaStream_t>(stream), who, objectsOnDevice != 0);
+}
+
+int lmcb_single_layer_kv_transfer_batched_kernel(
+    int type, int slotType, void* stream, const uint64_t* objectPtrs,
+    const int64_t* tokenOffsets, const int64_t* slotStarts, int32_t numObjects,
+    int objectsOnDevice, void* keyCachePtr, void* valueCachePtr, const void* slotmappings,
+    int64_t hiddenDims, int32_t totalTokens, int page2L, int tokenMajor,
+    int64_t pagedRowStride, int64_t numPagedRows) {
+  lmcb::clear_error();
+  const char* who = "single_layer_kv_transfer_batched";
+  if (numObjects < 0) {
+    return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": negative object count.");
+  }
+  if (numObjects == 0 || totalTokens == 0) return LMCB_OK;
+  const int64_t esz = lmcb::dtype_size(type);
+  const int64_t row = hiddenDims * esz;
+  TransferParams p{};
+  p.base_k = static_cast<uint8_t*>(keyCachePtr);
+  p.base_v = static_cast<uint8_t*>(valueCachePtr);
+  p.paged_row_stride = pagedRowStride > 0 ? pagedRowStride : row;
+  p.num_paged_rows = numPagedRows;
+  p.slots = slotmappings;
+  p.num_tokens = totalTokens;
+  p.num_layers = 1;
+  p.num_kv = 2;
+  p.row_bytes = esz == 0 ? 1 : row;
+  p.page2L = page2L ? 1 : 0;
+  p.obj_ptrs = objectPtrs;
+  p.obj_offsets = tokenOffsets;
+  p.obj_slot_starts = slotStarts;
+  p.num_objects = numObjects;
+  p.obj_token_major = tokenMajor ? 1 : 0;
+  return lmcb::launch_transfer(
+      p, type, slotType, lmcb::kBatchedDirect,
+      {static_cast<uint64_t>(row), reinterpret_cast<uint64_t>(keyCachePtr),
+       reinterpret_cast<uint64_t>(valueCachePtr), static_cast<uint64_t>(p.paged_row_stride)},
+      static_cast<cudaStream_t>(stream), who, objectsOnDevice != 0);
 }
 
 int lmcb_multi_layer_kv_store_staged(int type, int slotType, void* stream,

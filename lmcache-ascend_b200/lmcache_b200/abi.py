@@ -60,6 +60,11 @@ SIGNATURES: dict[str, tuple] = {
         [c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int,
          c_void_p, c_int64, c_int32, c_int32, c_int64, c_int32, c_int],
     ),
+    "lmcb_single_layer_kv_transfer_batched_kernel": (
+        c_int,
+        [c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int, c_void_p,
+         c_void_p, c_void_p, c_int64, c_int32, c_int, c_int, c_int64, c_int64],
+    ),
     "lmcb_single_layer_kv_transfer_kernel": (
         c_int,
         [c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int32,

@@ -160,6 +160,20 @@ class VLLMPagedMemLayerwiseGPUConnector:
         return torch.empty(self.get_shape(num_tokens), dtype=self.dtype,
                            device=self.kvcaches[0].device)
 
+    def _layer_batched(self, memory_objs_layer: Sequence[MemoryObj], layer_id: int,
+                       slot_mapping: torch.Tensor, starts: Sequence[int], ends: Sequence[int],
+                       direction: bool) -> None:
+        """One single_layer_kv_transfer_batched launch per residency group."""
+        groups: Dict[bool, list] = {}
+        for obj, s, e in zip(memory_objs_layer, starts, ends):
+            assert obj.tensor is not None
+            groups.setdefault(obj.tensor.is_cuda, []).append((obj.tensor, int(s), int(e)))
+        for items in groups.values():
+            c_ops.single_layer_kv_transfer_batched(
+                [t for t, _, _ in items], self.kvcaches[layer_id][0], self.kvcaches[layer_id][1],
+                slot_mapping, [s for _, s, _ in items], [e for _, _, e in items], direction,
+                True)
+
     def batched_to_gpu(self, starts: List[int], ends: List[int], **kwargs):
         """Generator: MemoryObjs -> paged cache, one layer per ``send``.
 
@@ -187,14 +201,15 @@ class VLLMPagedMemLayerwiseGPUConnector:
             if sync:
                 current_stream.wait_stream(self.load_stream)
             with torch.cuda.stream(self.load_stream):
-                for start, end, memory_obj in zip(starts, ends, memory_objs_layer):
-                    if self.use_gpu:
+                if self.use_gpu:
+                    for start, end, memory_obj in zip(starts, ends, memory_objs_layer):
                         tmp[start - offset : end - offset].copy_(memory_obj.tensor,
                                                                  non_blocking=True)
-                    else:
-                        c_ops.single_layer_kv_transfer(
-                            memory_obj.tensor, self.kvcaches[layer_id][0],
-                            self.kvcaches[layer_id][1], slot_mapping[start:end], False, True)
+                else:
+                    # every chunk of this layer in one launch (the reference
+                    # issues one single_layer_kv_transfer per chunk)
+                    self._layer_batched(memory_objs_layer, layer_id, slot_mapping, starts, ends,
+                                        False)
                 if self.use_gpu:
                     c_ops.single_layer_kv_transfer(
                         tmp, self.kvcaches[layer_id][0], self.kvcaches[layer_id][1],
@@ -231,15 +246,14 @@ class VLLMPagedMemLayerwiseGPUConnector:
                     c_ops.single_layer_kv_transfer(
                         tmp, self.kvcaches[layer_id][0], self.kvcaches[layer_id][1],
                         slot_mapping_full, True, True)
-                for start, end, memory_obj in zip(starts, ends, memory_objs_layer):
-                    assert memory_obj.tensor is not None
-                    if self.use_gpu:
+                if self.use_gpu:
+                    for start, end, memory_obj in zip(starts, ends, memory_objs_layer):
+                        assert memory_obj.tensor is not None
                         memory_obj.tensor.copy_(tmp[start - offset : end - offset],
                                                 non_blocking=True)
-                    else:
-                        c_ops.single_layer_kv_transfer(
-                            memory_obj.tensor, self.kvcaches[layer_id][0],
-                            self.kvcaches[layer_id][1], slot_mapping[start:end], True, True)
+                else:
+                    self._layer_batched(memory_objs_layer, layer_id, slot_mapping, starts, ends,
+                                        True)
             yield
             if sync:
                 self.store_stream.synchronize()

@@ -133,3 +133,47 @@ def test_connector_batched_round_trip(arena):
         assert torch.equal(fa[:, valid], fb[:, valid])
     arena.free(objs[0])
     arena.free(objs[2])
+
+
+@pytest.mark.parametrize("token_major", [True, False])
+@pytest.mark.parametrize("where", ["hbm", "pinned"])
+def test_single_layer_batched_matches_oracle(token_major, where, transfer_path, arena):
+    num_blocks, block_size, heads, hd = 64, 16, 8, 128
+    H = heads * hd
+    g = torch.Generator(device=DEV).manual_seed(44)
+    kc = torch.randn(num_blocks, block_size, heads, hd, generator=g, device=DEV).to(torch.bfloat16)
+    vc = torch.randn(num_blocks, block_size, heads, hd, generator=g, device=DEV).to(torch.bfloat16)
+    gc = torch.Generator().manual_seed(45)
+    slots = torch.randperm(num_blocks * block_size, generator=gc)[:1000].to(torch.int64)
+    slots[torch.randperm(1000, generator=gc)[:20]] = -1
+    sd = slots.to(DEV)
+    objs, handles = [], []
+    for s, e in RANGES:
+        shape = (e - s, 2, H) if token_major else (2, e - s, H)
+        if where == "hbm":
+            objs.append(torch.zeros(shape, dtype=torch.bfloat16, device=DEV))
+        else:
+            mo = arena.allocate(shape, torch.bfloat16)
+            mo.tensor.zero_()
+            handles.append(mo)
+            objs.append(mo.tensor)
+    c_ops.single_layer_kv_transfer_batched(objs, kc, vc, sd, [s for s, _ in RANGES],
+                                           [e for _, e in RANGES], True, token_major)
+    torch.cuda.synchronize()
+    k_np, v_np = bits(kc), bits(vc)
+    for obj, (s, e) in zip(objs, RANGES):
+        want = np.zeros(obj.shape, dtype=np.int16)
+        oracle.single_layer_kv_transfer(want, k_np, v_np, slots[s:e].numpy(), True, token_major)
+        assert np.array_equal(bits(obj), want)
+    kn, vn = torch.zeros_like(kc), torch.zeros_like(vc)
+    c_ops.single_layer_kv_transfer_batched(objs, kn, vn, sd, [s for s, _ in RANGES],
+                                           [e for _, e in RANGES], False, token_major)
+    torch.cuda.synchronize()
+    kw, vw = np.zeros_like(k_np), np.zeros_like(v_np)
+    for obj, (s, e) in zip(objs, RANGES):
+        oracle.single_layer_kv_transfer(bits(obj), kw, vw, slots[s:e].numpy(), False, token_major)
+    assert np.array_equal(bits(kn), kw)
+    assert np.array_equal(bits(vn), vw)
+    for mo in handles:
+        arena.free(mo)
+    assert c_ops.device_status(torch.cuda.current_device()) == 0
