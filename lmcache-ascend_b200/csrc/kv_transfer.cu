@@ -577,11 +577,15 @@ int env_int(const char* name, int dflt) {
 // Ring geometry; LMCB_BULK_STAGES / LMCB_BULK_STAGE_KB / LMCB_BULK_CTAS_PER_SM
 // override the defaults (tuning only; read on every call so a process can
 // compare settings).
-BulkConfig bulk_config() {
+// Defaults from sweeps on B200: rows of 1 KB and more stream best with
+// 3 CTAs/SM x 4 stages x 16 KB; short rows (e.g. a 256-byte TP-8 shard row)
+// need more issuing warps: 4 CTAs/SM x 6 stages x 8 KB.
+BulkConfig bulk_config(int64_t row_bytes) {
+  const bool short_rows = row_bytes <= 512;
   BulkConfig c;
-  c.stages = env_int("LMCB_BULK_STAGES", 4);
-  c.stage_kb = env_int("LMCB_BULK_STAGE_KB", 16);
-  c.ctas_per_sm = env_int("LMCB_BULK_CTAS_PER_SM", 3);
+  c.stages = env_int("LMCB_BULK_STAGES", short_rows ? 6 : 4);
+  c.stage_kb = env_int("LMCB_BULK_STAGE_KB", short_rows ? 8 : 16);
+  c.ctas_per_sm = env_int("LMCB_BULK_CTAS_PER_SM", short_rows ? 4 : 3);
   if (c.stages < 2) c.stages = 2;
   if (c.stages > kBulkMaxStages) c.stages = kBulkMaxStages;
   if (c.stage_kb < 4) c.stage_kb = 4;
@@ -743,7 +747,7 @@ int launch_transfer(TransferParams p, int type, int slot_type, int mode,
     if (std::strcmp(v, "bulk") == 0) return 2;
     return 0;
   }();
-  const BulkConfig bc = bulk_config();
+  const BulkConfig bc = bulk_config(p.row_bytes);
   const int64_t stage_bytes = static_cast<int64_t>(bc.stage_kb) * 1024;
   const bool lmc_on_device = batched_mode(mode) ? objects_on_device : is_device_memory(p.lmc);
   const bool bulk_ok = vec == 16 && p.row_bytes % 16 == 0 && p.row_bytes <= stage_bytes &&
