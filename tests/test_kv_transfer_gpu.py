@@ -441,11 +441,14 @@ def test_workload_full_size(name, memobj_on, pin_alloc):
     torch.cuda.empty_cache()
 
 
-@pytest.mark.parametrize("ctas_per_sm", ["1", "3"])
+@pytest.mark.parametrize("ctas_per_sm", ["1", "3", "default-path"])
 def test_large_single_launch(ctas_per_sm, monkeypatch):
     """One launch of 262144 rows: each bulk-copy CTA resolves many 256-row
     batches and its ring wraps many times."""
-    monkeypatch.setenv("LMCB_BULK_CTAS_PER_SM", ctas_per_sm)
+    if ctas_per_sm != "default-path":
+        monkeypatch.setenv("LMCB_BULK_CTAS_PER_SM", ctas_per_sm)
+        # large launches default to the vectorised kernel; force the bulk ring
+        monkeypatch.setenv("LMCB_TRANSFER_PATH", "bulk")
     num_layers, num_blocks, block_size, heads, hd, T = 32, 512, 16, 8, 128, 4096
     pbs = num_blocks * block_size
     kv = kv_list(num_layers, num_blocks, block_size, heads, hd, torch.bfloat16, seed=21)
