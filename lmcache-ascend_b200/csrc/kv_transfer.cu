@@ -138,6 +138,9 @@ template <> struct VecType<2> { using T = uint16_t; };
 // the next kernel be scheduled while this one runs. Both are no-ops when the
 // launch carries no programmatic-serialization attribute.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void prefetch_l2(const void* ptr) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
+}
 __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
@@ -505,17 +508,29 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b) {
     s_len[st * 32 + lane] = bytes;
   };
 
-  // Under programmatic dependent launch the first batch is resolved while the
-  // previous kernel in the stream is still finishing: resolution only reads
-  // the slot mapping and the layer-base array, which no transfer kernel
-  // writes, and it touches no payload. Only slots that are bounds-checked
-  // (a known paged row count) are resolved this early; payload reads and
-  // writes all come after griddepcontrol.wait.
-  if (p.num_paged_rows > 0 && n_rows > 0) {
-    cur_b0 = 0;
-    cur_n = min(kBatchRows, n_rows);
-    cur_next = 0;
-    resolve_batch(cur_b0, cur_n);
+  // Under programmatic dependent launch this CTA can start while the previous
+  // kernel in the stream is still running, and none of that kernel's writes
+  // is guaranteed visible before griddepcontrol.wait -- the slot mapping and
+  // the layer-base array included, since a caller may build either on the
+  // GPU right before the transfer. Before the wait the CTA therefore only
+  // prefetches its first batch's slot ids and layer bases into L2 (a hint
+  // that loads nothing into registers; L2 sees the previous kernel's writes).
+  if (!batched_mode(MODE) && n_rows > 0) {
+    constexpr int kPer = kBatchRows / 32;
+    const int32_t n0 = min(kBatchRows, n_rows);
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int idx = lane + 32 * j;
+      if (idx < n0) {
+        const uint32_t r = static_cast<uint32_t>(r_begin + idx);
+        const uint32_t q = b.div_tokens.div(r);
+        const int tok = static_cast<int>(r - q * b.div_tokens.d);
+        const int kv = static_cast<int>(b.div_layers.div(q));
+        const int layer = static_cast<int>(q - kv * b.div_layers.d);
+        prefetch_l2(slots + tok);
+        if (!paged_direct(MODE)) prefetch_l2((kv == 0 ? p.ptrs_k : p.ptrs_v) + layer);
+      }
+    }
   }
   pdl_wait();
   pdl_launch_dependents();

@@ -309,6 +309,55 @@ def test_unilateral(transfer_path):
         assert np.array_equal(bits(a), b)
 
 
+def test_inputs_written_by_the_preceding_kernel(transfer_path):
+    """The slot mapping and the layer-pointer array are rewritten by a torch
+    kernel right before every transfer on the same stream (as when an engine
+    builds the slot mapping on the GPU). The transfer kernels start early under
+    programmatic dependent launch, so this pins that they read neither input
+    before the previous kernel's writes are visible."""
+    L, nb, bs, heads, hd, T, n = 8, 256, 16, 8, 128, 256, 12
+    pbs = nb * bs
+    kv_a = kv_list(L, nb, bs, heads, hd, torch.bfloat16, seed=51)
+    kv_b = kv_list(L, nb, bs, heads, hd, torch.bfloat16, seed=52)
+    ptr_src = [ptrs_of(kv_a), ptrs_of(kv_b)]
+    perm = torch.randperm(pbs, generator=torch.Generator().manual_seed(53))
+    slot_sets = [perm[i * T:(i + 1) * T].to(torch.int32) for i in range(n)]
+    slot_src = [s.to(DEV) for s in slot_sets]
+    sd = torch.full((T,), -1, dtype=torch.int64, device=DEV)
+    ptrs = torch.zeros(L, dtype=torch.int64, device=DEV)
+    objs = [torch.zeros([2, L, T, heads * hd], dtype=torch.bfloat16, device=DEV) for _ in range(n)]
+    torch.cuda.synchronize()
+    for i in range(n):
+        sd.copy_(slot_src[i])  # int32 -> int64: an elementwise kernel
+        torch.add(ptr_src[i % 2], 0, out=ptrs)
+        c_ops.multi_layer_kv_transfer(objs[i], ptrs, sd, kv_a[0].device, pbs, True, False)
+    torch.cuda.synchronize()
+    np_a, np_b = [bits(t) for t in kv_a], [bits(t) for t in kv_b]
+    for i in range(n):
+        want = np.zeros(objs[i].shape, dtype=np.int16)
+        oracle.multi_layer_kv_transfer(want, np_a if i % 2 == 0 else np_b,
+                                       slot_sets[i].numpy().astype(np.int64), pbs, True, False)
+        assert np.array_equal(bits(objs[i]), want), i
+    # retrieve each object back into fresh caches, the same way
+    new_a = [torch.zeros_like(t) for t in kv_a]
+    new_b = [torch.zeros_like(t) for t in kv_b]
+    new_src = [ptrs_of(new_a), ptrs_of(new_b)]
+    torch.cuda.synchronize()
+    for i in range(n):
+        sd.copy_(slot_src[i])
+        torch.add(new_src[i % 2], 0, out=ptrs)
+        c_ops.multi_layer_kv_transfer(objs[i], ptrs, sd, kv_a[0].device, pbs, False, False)
+    torch.cuda.synchronize()
+    want_a = [np.zeros_like(a) for a in np_a]
+    want_b = [np.zeros_like(b) for b in np_b]
+    for i in range(n):
+        oracle.multi_layer_kv_transfer(bits(objs[i]), want_a if i % 2 == 0 else want_b,
+                                       slot_sets[i].numpy().astype(np.int64), pbs, False, False)
+    for got, want in zip(new_a + new_b, want_a + want_b):
+        assert np.array_equal(bits(got), want)
+    assert c_ops.device_status(torch.cuda.current_device()) == 0
+
+
 def test_empty_and_all_skipped():
     kv = kv_list(2, 8, 16, 8, 128, torch.bfloat16, seed=1)
     ptrs = ptrs_of(kv)
