@@ -20,8 +20,12 @@
 //   encode/decode  one thread per (layer, channel) stream, 32 consecutive
 //                  channels per warp so symbol reads and writes of one token
 //                  row are coalesced; the CTA's CDF rows are staged in shared
-//                  memory; symbols pass through a shared-memory tile of
-//                  kTokTile tokens. The coder itself is sequential per stream.
+//                  memory, transposed so probes are bank-conflict free. The
+//                  coder itself is sequential per stream, so both kernels are
+//                  bound by the latency of one symbol step: encode prefetches
+//                  symbols several tokens ahead, decode loads the next input
+//                  byte ahead and probes two search levels per shared-memory
+//                  round trip.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -123,23 +127,23 @@ cdf_kernel(const uint8_t* __restrict__ sym, uint16_t* __restrict__ cdf, int T, i
 // encode / decode
 // ---------------------------------------------------------------------------
 
-constexpr int kCoderThreads = 128;  // channels per CTA
-constexpr int kTokTile = 32;        // tokens staged per shared-memory tile
+constexpr int kCoderThreads = 128;  // channels (streams) per CTA
+constexpr int kSymAhead = 8;        // encode: symbols prefetched per stream
 
-// Shared memory: CDF rows [kCoderThreads][max_bins + 1] (uint16), then the
-// symbol tile [kTokTile][kCoderThreads] (uint8).
+// Shared memory holds the CTA's CDF rows transposed and widened to 32 bits:
+// s_cdf[k * kCoderThreads + i] = cdf[k] of the CTA's i-th channel. Each lane
+// owns one bank, so a warp's probes never conflict whatever bin each lane
+// looks at.
 inline size_t coder_smem_bytes(int max_bins) {
-  size_t cdf = static_cast<size_t>(kCoderThreads) * (max_bins + 1) * sizeof(uint16_t);
-  cdf = (cdf + 15) & ~size_t(15);
-  return cdf + static_cast<size_t>(kTokTile) * kCoderThreads;
+  return static_cast<size_t>(kCoderThreads) * (max_bins + 1) * sizeof(uint32_t);
 }
 
-__device__ __forceinline__ void load_cdf_rows(uint16_t* s_cdf, const uint16_t* cdf, int l, int c0,
+__device__ __forceinline__ void load_cdf_rows(uint32_t* s_cdf, const uint16_t* cdf, int l, int c0,
                                               int C, int max_bins) {
-  const int n_ch = min(kCoderThreads, C - c0);
-  const int64_t n = static_cast<int64_t>(n_ch) * (max_bins + 1);
-  const uint16_t* src = cdf + (static_cast<int64_t>(l) * C + c0) * (max_bins + 1);
-  for (int64_t i = threadIdx.x; i < n; i += kCoderThreads) s_cdf[i] = src[i];
+  const int c = c0 + static_cast<int>(threadIdx.x);
+  if (c >= C) return;
+  const uint16_t* row = cdf + (static_cast<int64_t>(l) * C + c) * (max_bins + 1);
+  for (int k = 0; k <= max_bins; ++k) s_cdf[k * kCoderThreads + threadIdx.x] = row[k];
 }
 
 struct ByteSink {
@@ -176,21 +180,25 @@ struct ByteSink {
   }
 };
 
+// One stream per thread, 32 consecutive channels per warp. Symbols are read
+// straight from global memory (a warp reads one 32-byte run of a token row)
+// kSymAhead tokens ahead of their use, so their latency overlaps the coding
+// of the tokens before them; no block-wide barrier after the CDF load.
 __global__ void __launch_bounds__(kCoderThreads)
 encode_kernel(const uint16_t* __restrict__ cdf, const uint8_t* __restrict__ sym,
               uint8_t* __restrict__ out, int32_t* __restrict__ lengths, int T, int C,
               int max_bins, int64_t stride, unsigned int* status) {
   extern __shared__ __align__(16) uint8_t smem[];
-  uint16_t* s_cdf = reinterpret_cast<uint16_t*>(smem);
-  uint8_t* s_sym = smem + ((static_cast<size_t>(kCoderThreads) * (max_bins + 1) * 2 + 15) & ~size_t(15));
+  uint32_t* s_cdf = reinterpret_cast<uint32_t*>(smem);
   const int l = blockIdx.y;
   const int c0 = blockIdx.x * kCoderThreads;
   const int tid = threadIdx.x;
   const int c = c0 + tid;
-  const bool active = c < C;
   load_cdf_rows(s_cdf, cdf, l, c0, C, max_bins);
+  __syncthreads();
+  if (c >= C) return;
 
-  const uint16_t* my_cdf = s_cdf + tid * (max_bins + 1);
+  const uint32_t* my_cdf = s_cdf + tid;  // my_cdf[k * kCoderThreads] = cdf[k]
   const int64_t stream = static_cast<int64_t>(l) * C + c;
   ByteSink sink;
   sink.out = out + stream * stride;
@@ -201,142 +209,270 @@ encode_kernel(const uint16_t* __restrict__ cdf, const uint8_t* __restrict__ sym,
   sink.overflow = false;
   uint32_t low = 0, range = 0xFFFFFFFFu;
   bool oor = false;
-  const uint8_t* base = sym + static_cast<int64_t>(l) * T * C;
-  const int n_ch = min(kCoderThreads, C - c0);
+  const uint8_t* in = sym + static_cast<int64_t>(l) * T * C + c;
 
-  for (int t0 = 0; t0 < T; t0 += kTokTile) {
-    const int nt = min(kTokTile, T - t0);
-    __syncthreads();  // previous tile consumed (and the CDF rows loaded)
-    for (int i = tid; i < nt * kCoderThreads; i += kCoderThreads) {
-      const int tt = i / kCoderThreads;
-      const int cc = i - tt * kCoderThreads;
-      if (cc < n_ch) s_sym[tt * kCoderThreads + cc] = base[static_cast<int64_t>(t0 + tt) * C + c0 + cc];
+  auto code_symbol = [&](uint32_t s) {
+    if (s >= static_cast<uint32_t>(max_bins)) {
+      oor = true;
+      s = max_bins - 1;
     }
-    __syncthreads();
-    if (active) {
-      for (int tt = 0; tt < nt; ++tt) {
-        uint32_t s = s_sym[tt * kCoderThreads + tid];
-        if (s >= static_cast<uint32_t>(max_bins)) {
-          oor = true;
-          s = max_bins - 1;
-        }
-        const uint32_t lo = my_cdf[s];
-        const uint32_t hi = my_cdf[s + 1];
-        const uint32_t r = range >> kProbBits;
-        low += lo * r;
-        range = r * (hi - lo);
-        // At most four byte shifts are ever needed; the bound only guards
-        // against a state the coder cannot reach.
-        for (int it = 0; it < kMaxRenorm; ++it) {
-          if ((low ^ (low + range)) >= kTop) {
-            if (range >= kBot) break;
-            range = (0u - low) & (kBot - 1u);
-          }
-          sink.put(low >> 24);
-          low <<= 8;
-          range <<= 8;
-        }
+    const uint32_t lo = my_cdf[s * kCoderThreads];
+    const uint32_t hi = my_cdf[(s + 1) * kCoderThreads];
+    const uint32_t r = range >> kProbBits;
+    low += lo * r;
+    range = r * (hi - lo);
+    // At most four byte shifts are ever needed; the bound only guards
+    // against a state the coder cannot reach.
+    for (int it = 0; it < kMaxRenorm; ++it) {
+      if ((low ^ (low + range)) >= kTop) {
+        if (range >= kBot) break;
+        range = (0u - low) & (kBot - 1u);
+      }
+      sink.put(low >> 24);
+      low <<= 8;
+      range <<= 8;
+    }
+  };
+
+  uint32_t cur[kSymAhead];
+#pragma unroll
+  for (int j = 0; j < kSymAhead; ++j) {
+    cur[j] = j < T ? static_cast<uint32_t>(__ldg(in + static_cast<int64_t>(j) * C)) : 0u;
+  }
+  int t0 = 0;
+  // Whole blocks of kSymAhead tokens: the next block's symbols are loaded,
+  // then this block's are coded with no per-token bounds test.
+  for (; t0 + kSymAhead <= T; t0 += kSymAhead) {
+    uint32_t nxt[kSymAhead];
+#pragma unroll
+    for (int j = 0; j < kSymAhead; ++j) {
+      const int t = t0 + kSymAhead + j;
+      nxt[j] = t < T ? static_cast<uint32_t>(__ldg(in + static_cast<int64_t>(t) * C)) : 0u;
+    }
+#pragma unroll
+    for (int j = 0; j < kSymAhead; ++j) code_symbol(cur[j]);
+#pragma unroll
+    for (int j = 0; j < kSymAhead; ++j) cur[j] = nxt[j];
+  }
+  // The last T % kSymAhead tokens (already in cur).
+#pragma unroll
+  for (int j = 0; j < kSymAhead; ++j) {
+    if (t0 + j < T) code_symbol(cur[j]);
+  }
+  for (int i = 0; i < 4; ++i) {
+    sink.put(low >> 24);
+    low <<= 8;
+  }
+  sink.flush();
+  lengths[stream] = sink.overflow ? -1 : static_cast<int32_t>(sink.pos);
+  if (sink.overflow) raise_flag(status, LMCB_DEVICE_FLAG_STREAM_OVERFLOW);
+  if (oor) raise_flag(status, LMCB_DEVICE_FLAG_SYMBOL_OUT_OF_RANGE);
+}
+
+// One level of the decoder's symbol search: the largest a with cdf[a] <= v,
+// v = min((code - low) / r, kTotal - 1), by the halving search
+// m = (a + b) / 2 over [a, b). For integers cdf[m] <= floor(x / r) exactly
+// when cdf[m] * r <= x, and cdf[m] <= kTotal - 1 is the clamp, so a probe is
+// a product and two compares (the product of a value below 2^15 and r below
+// 2^17 fits 32 bits). lo / hi carry cdf[a] / cdf[b] (the last accepted and
+// the last rejected probe), so the coder needs no separate loads of them.
+__device__ __forceinline__ bool probe_ok(uint32_t cm, uint32_t r, uint32_t x) {
+  return cm < kTotal && cm * r <= x;
+}
+
+// Any alphabet size: the halving search over [0, max_bins), two levels per
+// shared-memory round trip (the probe m and both probes the next level can
+// take are loaded together, then the taken one is kept). The probe sequence
+// is exactly that of the one-level search.
+__device__ __forceinline__ uint32_t search_any(const uint32_t* my_cdf, uint32_t r, uint32_t x,
+                                               int max_bins, int depth, uint32_t& lo,
+                                               uint32_t& hi) {
+  uint32_t a = 0, b = static_cast<uint32_t>(max_bins);
+  for (int lvl = 0; lvl < depth; lvl += 2) {
+    if (b - a <= 1) break;
+    const uint32_t m = (a + b) >> 1;
+    const uint32_t m_lo = (a + m) >> 1;  // next probe if cdf[m] is rejected
+    const uint32_t m_hi = (m + b) >> 1;  // next probe if cdf[m] is accepted
+    const uint32_t cm = my_cdf[m * kCoderThreads];
+    const uint32_t c_lo = my_cdf[m_lo * kCoderThreads];
+    const uint32_t c_hi = my_cdf[m_hi * kCoderThreads];
+    const bool ok = probe_ok(cm, r, x);
+    if (ok) {
+      a = m;
+      lo = cm;
+    } else {
+      b = m;
+      hi = cm;
+    }
+    if (b - a > 1) {
+      const uint32_t m2 = ok ? m_hi : m_lo;
+      const uint32_t c2 = ok ? c_hi : c_lo;
+      if (probe_ok(c2, r, x)) {
+        a = m2;
+        lo = c2;
+      } else {
+        b = m2;
+        hi = c2;
       }
     }
   }
-  if (active) {
-    for (int i = 0; i < 4; ++i) {
-      sink.put(low >> 24);
-      low <<= 8;
-    }
-    sink.flush();
-    lengths[stream] = sink.overflow ? -1 : static_cast<int32_t>(sink.pos);
-    if (sink.overflow) raise_flag(status, LMCB_DEVICE_FLAG_STREAM_OVERFLOW);
-    if (oor) raise_flag(status, LMCB_DEVICE_FLAG_SYMBOL_OUT_OF_RANGE);
+  return a;
+}
+
+// Alphabet of 2^D symbols: every interval of the halving search is a power
+// of two, so level k (k = D-1 .. 0) probes a + 2^k and the search unrolls
+// with no bounds tests and no branches; offsets from a are immediates. Two
+// levels share one shared-memory round trip as in search_any.
+template <int D>
+__device__ __forceinline__ uint32_t search_pow2(const uint32_t* my_cdf, uint32_t r, uint32_t x,
+                                                uint32_t& lo, uint32_t& hi) {
+  uint32_t a = 0;
+#pragma unroll
+  for (int k = D - 1; k >= 1; k -= 2) {
+    const uint32_t* row = my_cdf + a * kCoderThreads;
+    const uint32_t cm = row[(1u << k) * kCoderThreads];
+    const uint32_t c_lo = row[(1u << (k - 1)) * kCoderThreads];
+    const uint32_t c_hi = row[((1u << k) + (1u << (k - 1))) * kCoderThreads];
+    const bool ok = probe_ok(cm, r, x);
+    lo = ok ? cm : lo;
+    hi = ok ? hi : cm;
+    const uint32_t a1 = ok ? a + (1u << k) : a;
+    const uint32_t c2 = ok ? c_hi : c_lo;
+    const bool ok2 = probe_ok(c2, r, x);
+    lo = ok2 ? c2 : lo;
+    hi = ok2 ? hi : c2;
+    a = ok2 ? a1 + (1u << (k - 1)) : a1;
   }
+  if (D & 1) {
+    const uint32_t c1 = my_cdf[(a + 1) * kCoderThreads];
+    const bool ok = probe_ok(c1, r, x);
+    lo = ok ? c1 : lo;
+    hi = ok ? hi : c1;
+    a = ok ? a + 1 : a;
+  }
+  return a;
 }
 
 // Decodes with streams either at fixed stride (ends == nullptr) or
-// concatenated with inclusive end offsets.
+// concatenated with inclusive end offsets. `depth` = ceil(log2(max_bins)),
+// the most levels the halving search can take; kPow2Depth = depth when
+// max_bins is a power of two (the unrolled search), -1 otherwise.
+template <int kPow2Depth>
 __global__ void __launch_bounds__(kCoderThreads)
 decode_kernel(const uint16_t* __restrict__ cdf, const uint8_t* __restrict__ in,
               const int32_t* __restrict__ lengths, const int64_t* __restrict__ ends,
-              uint8_t* __restrict__ sym, int T, int C, int max_bins, int64_t stride,
+              uint8_t* __restrict__ sym, int T, int C, int max_bins, int depth, int64_t stride,
               int64_t total_bytes) {
   extern __shared__ __align__(16) uint8_t smem[];
-  uint16_t* s_cdf = reinterpret_cast<uint16_t*>(smem);
-  uint8_t* s_sym = smem + ((static_cast<size_t>(kCoderThreads) * (max_bins + 1) * 2 + 15) & ~size_t(15));
+  uint32_t* s_cdf = reinterpret_cast<uint32_t*>(smem);
   const int l = blockIdx.y;
   const int c0 = blockIdx.x * kCoderThreads;
   const int tid = threadIdx.x;
   const int c = c0 + tid;
-  const bool active = c < C;
   load_cdf_rows(s_cdf, cdf, l, c0, C, max_bins);
+  __syncthreads();
+  if (c >= C) return;
 
-  const uint16_t* my_cdf = s_cdf + tid * (max_bins + 1);
+  const uint32_t* my_cdf = s_cdf + tid;  // my_cdf[k * kCoderThreads] = cdf[k]
   const int64_t stream = static_cast<int64_t>(l) * C + c;
-  const uint8_t* src = nullptr;
-  int64_t len = 0;
-  if (active) {
-    if (ends == nullptr) {
-      src = in + stream * stride;
-      len = lengths[stream];
-      if (len < 0) len = 0;
-      if (len > stride) len = stride;
-    } else {
-      // Offsets are clamped to the buffer, so a bad prefix sum cannot read
-      // outside it.
-      int64_t start = stream == 0 ? 0 : ends[stream - 1];
-      int64_t end = ends[stream];
-      start = start < 0 ? 0 : (start > total_bytes ? total_bytes : start);
-      end = end < start ? start : (end > total_bytes ? total_bytes : end);
-      src = in + start;
-      len = end - start;
-    }
+  const uint8_t* src;
+  int64_t len;
+  if (ends == nullptr) {
+    src = in + stream * stride;
+    len = lengths[stream];
+    if (len < 0) len = 0;
+    if (len > stride) len = stride;
+  } else {
+    // Offsets are clamped to the buffer, so a bad prefix sum cannot read
+    // outside it.
+    int64_t start = stream == 0 ? 0 : ends[stream - 1];
+    int64_t end = ends[stream];
+    start = start < 0 ? 0 : (start > total_bytes ? total_bytes : start);
+    end = end < start ? start : (end > total_bytes ? total_bytes : end);
+    src = in + start;
+    len = end - start;
   }
-  int64_t pos = 0;
-  auto next = [&]() -> uint32_t {
-    const uint32_t b = pos < len ? static_cast<uint32_t>(__ldg(src + pos)) : 0u;
-    ++pos;
-    return b;
+  // Bytes past the stream's end read as zero. The next byte is always loaded
+  // one ahead of its use.
+  auto fetch = [&](int64_t i) -> uint32_t {
+    return i < len ? static_cast<uint32_t>(__ldg(src + i)) : 0u;
   };
-  uint32_t low = 0, range = 0xFFFFFFFFu, code = 0;
-  if (active) {
-    for (int i = 0; i < 4; ++i) code = (code << 8) | next();
-  }
-  uint8_t* base = sym + static_cast<int64_t>(l) * T * C;
-  const int n_ch = min(kCoderThreads, C - c0);
+  uint32_t code = 0;
+  for (int i = 0; i < 4; ++i) code = (code << 8) | fetch(i);
+  int64_t pos = 4;
+  uint32_t ahead = fetch(pos);
+  uint32_t low = 0, range = 0xFFFFFFFFu;
+  const uint32_t cdf_first = my_cdf[0];
+  const uint32_t cdf_last = my_cdf[max_bins * kCoderThreads];
+  uint8_t* dst = sym + static_cast<int64_t>(l) * T * C + c;
 
-  for (int t0 = 0; t0 < T; t0 += kTokTile) {
-    const int nt = min(kTokTile, T - t0);
-    if (active) {
-      for (int tt = 0; tt < nt; ++tt) {
-        const uint32_t r = range >> kProbBits;
-        uint32_t v = (code - low) / r;
-        if (v >= kTotal) v = kTotal - 1;
-        int a = 0, b = max_bins;  // cdf[a] <= v < cdf[b]
-        while (b - a > 1) {
-          const int m = (a + b) >> 1;
-          if (my_cdf[m] <= v) a = m; else b = m;
-        }
-        const uint32_t lo = my_cdf[a];
-        const uint32_t hi = my_cdf[a + 1];
-        low += lo * r;
-        range = r * (hi - lo);
-        for (int it = 0; it < kMaxRenorm; ++it) {
-          if ((low ^ (low + range)) >= kTop) {
-            if (range >= kBot) break;
-            range = (0u - low) & (kBot - 1u);
-          }
-          code = (code << 8) | next();
-          low <<= 8;
-          range <<= 8;
-        }
-        s_sym[tt * kCoderThreads + tid] = static_cast<uint8_t>(a);
+  for (int t = 0; t < T; ++t) {
+    const uint32_t r = range >> kProbBits;
+    const uint32_t x = code - low;
+    uint32_t lo = cdf_first, hi = cdf_last;
+    const uint32_t a = kPow2Depth >= 0
+                           ? search_pow2<(kPow2Depth >= 0 ? kPow2Depth : 0)>(my_cdf, r, x, lo, hi)
+                           : search_any(my_cdf, r, x, max_bins, depth, lo, hi);
+    low += lo * r;
+    range = r * (hi - lo);
+    for (int it = 0; it < kMaxRenorm; ++it) {
+      if ((low ^ (low + range)) >= kTop) {
+        if (range >= kBot) break;
+        range = (0u - low) & (kBot - 1u);
       }
+      code = (code << 8) | ahead;
+      ++pos;
+      ahead = fetch(pos);
+      low <<= 8;
+      range <<= 8;
     }
-    __syncthreads();
-    for (int i = tid; i < nt * kCoderThreads; i += kCoderThreads) {
-      const int tt = i / kCoderThreads;
-      const int cc = i - tt * kCoderThreads;
-      if (cc < n_ch) base[static_cast<int64_t>(t0 + tt) * C + c0 + cc] = s_sym[tt * kCoderThreads + cc];
-    }
-    __syncthreads();
+    dst[static_cast<int64_t>(t) * C] = static_cast<uint8_t>(a);
+  }
+}
+
+int search_depth(int max_bins) {
+  int d = 0;
+  while ((1 << d) < max_bins) ++d;
+  return d;
+}
+
+struct DecodeArgs {
+  const uint16_t* cdf;
+  const uint8_t* in;
+  const int32_t* lengths;  // fixed-stride streams, or
+  const int64_t* ends;     // concatenated streams
+  uint8_t* sym;
+  int L, T, C, max_bins;
+  int64_t stride, total_bytes;
+};
+
+inline size_t coder_smem_cap();
+
+template <int kPow2Depth>
+cudaError_t launch_decode_as(const DecodeArgs& a, cudaStream_t stream) {
+  const size_t smem = coder_smem_bytes(a.max_bins);
+  cudaError_t err = ensure_smem_limit<&decode_kernel<kPow2Depth>>(smem, coder_smem_cap());
+  if (err != cudaSuccess) return err;
+  const dim3 grid((a.C + kCoderThreads - 1) / kCoderThreads, a.L);
+  decode_kernel<kPow2Depth><<<grid, kCoderThreads, smem, stream>>>(
+      a.cdf, a.in, a.lengths, a.ends, a.sym, a.T, a.C, a.max_bins, search_depth(a.max_bins),
+      a.stride, a.total_bytes);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream) {
+  const int d = search_depth(a.max_bins);
+  if ((1 << d) != a.max_bins) return launch_decode_as<-1>(a, stream);
+  switch (d) {
+    case 0: return launch_decode_as<0>(a, stream);
+    case 1: return launch_decode_as<1>(a, stream);
+    case 2: return launch_decode_as<2>(a, stream);
+    case 3: return launch_decode_as<3>(a, stream);
+    case 4: return launch_decode_as<4>(a, stream);
+    case 5: return launch_decode_as<5>(a, stream);
+    case 6: return launch_decode_as<6>(a, stream);
+    case 7: return launch_decode_as<7>(a, stream);
+    default: return launch_decode_as<8>(a, stream);
   }
 }
 
@@ -417,13 +553,10 @@ int lmcb_decode(const int16_t* cdf, const uint8_t* bytestreams, const int32_t* l
   if (cdf == nullptr || bytestreams == nullptr || lengths == nullptr || output == nullptr) {
     return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT, "decode: NULL pointer.");
   }
-  const size_t smem = lmcb::coder_smem_bytes(maxBins);
-  LMCB_CUDA_TRY(lmcb::ensure_smem_limit<&lmcb::decode_kernel>(smem, lmcb::coder_smem_cap()));
-  dim3 grid((numChannels + lmcb::kCoderThreads - 1) / lmcb::kCoderThreads, numLayers);
-  lmcb::decode_kernel<<<grid, lmcb::kCoderThreads, smem, static_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const uint16_t*>(cdf), bytestreams, lengths, nullptr,
-      reinterpret_cast<uint8_t*>(output), numTokens, numChannels, maxBins, bufferStride, 0);
-  LMCB_CUDA_TRY(cudaGetLastError());
+  const lmcb::DecodeArgs args{reinterpret_cast<const uint16_t*>(cdf), bytestreams, lengths,
+                              nullptr, reinterpret_cast<uint8_t*>(output), numLayers, numTokens,
+                              numChannels, maxBins, bufferStride, 0};
+  LMCB_CUDA_TRY(lmcb::launch_decode(args, static_cast<cudaStream_t>(stream)));
   return LMCB_OK;
 }
 
@@ -438,13 +571,10 @@ int lmcb_decode_prefsum(const int16_t* cdf, const uint8_t* bytestreams, int64_t 
       output == nullptr || streamBytes < 0) {
     return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT, "decode_prefsum: NULL pointer or negative size.");
   }
-  const size_t smem = lmcb::coder_smem_bytes(maxBins);
-  LMCB_CUDA_TRY(lmcb::ensure_smem_limit<&lmcb::decode_kernel>(smem, lmcb::coder_smem_cap()));
-  dim3 grid((numChannels + lmcb::kCoderThreads - 1) / lmcb::kCoderThreads, numLayers);
-  lmcb::decode_kernel<<<grid, lmcb::kCoderThreads, smem, static_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const uint16_t*>(cdf), bytestreams, nullptr, endOffsets,
-      reinterpret_cast<uint8_t*>(output), numTokens, numChannels, maxBins, 0, streamBytes);
-  LMCB_CUDA_TRY(cudaGetLastError());
+  const lmcb::DecodeArgs args{reinterpret_cast<const uint16_t*>(cdf), bytestreams, nullptr,
+                              endOffsets, reinterpret_cast<uint8_t*>(output), numLayers,
+                              numTokens, numChannels, maxBins, 0, streamBytes};
+  LMCB_CUDA_TRY(lmcb::launch_decode(args, static_cast<cudaStream_t>(stream)));
   return LMCB_OK;
 }
 

@@ -106,3 +106,29 @@ def test_empty_token_axis():
     lengths = torch.zeros((2, 5), dtype=torch.int32, device=DEV)
     c_ops.encode_fast_new(cdf, sym_dev, out, lengths)
     assert (lengths.cpu() == 4).all()
+
+
+@pytest.mark.parametrize("max_bins", [32, 21, 256, 2])
+def test_decode_of_arbitrary_bytes_matches_oracle(max_bins):
+    """Random bytes decoded with valid CDFs: the decoder's search sees values
+    of (code - low) / r at and above 2^15 (the clamp), and every length from
+    empty to the full capacity. Symbols must still match the oracle's."""
+    L, T, C = 2, 300, 70
+    rng = np.random.default_rng(max_bins)
+    sym = symbols(max_bins, L, T, C, max_bins)
+    cdf = cg.calculate_cdf(sym, max_bins)
+    cap = 96
+    streams = rng.integers(0, 256, size=(L, C, cap), dtype=np.uint8)
+    lengths = rng.integers(0, cap + 1, size=(L, C)).astype(np.int32)
+    lengths[0, :3] = [0, cap, 4]
+    want = cg.decode(cdf, streams, lengths, T)
+    dec = torch.zeros((L, T, C), dtype=torch.int8, device=DEV)
+    c_ops.decode_fast_new(torch.from_numpy(cdf).to(DEV), torch.from_numpy(streams).to(DEV),
+                          torch.from_numpy(lengths).to(DEV), dec)
+    assert np.array_equal(dec.cpu().numpy().view(np.uint8), want)
+    cat, ends = cg.concat_streams(streams, lengths)
+    want2 = cg.decode_prefsum(cdf, cat, ends, T)
+    dec2 = torch.zeros_like(dec)
+    c_ops.decode_fast_prefsum(torch.from_numpy(cdf).to(DEV), torch.from_numpy(cat).to(DEV),
+                              torch.from_numpy(ends).to(DEV), dec2)
+    assert np.array_equal(dec2.cpu().numpy().view(np.uint8), want2)
