@@ -396,18 +396,20 @@ def run_ours(args):
     with torch.cuda.graph(g2, capture_error_mode="thread_local"):
         cap = torch.cuda.current_stream()
         side_hbm.wait_stream(cap)
-        stored = []
-        for i in range(n_chunks):
-            c_ops.multi_layer_kv_transfer(hbm_objs[i], ptrs, dev_chunks[i], dev, pbs, True,
-                                          spec.use_mla)
-            ev = torch.cuda.Event()
-            ev.record(cap)
-            stored.append(ev)
-        with torch.cuda.stream(side_hbm):
-            for i in range(n_chunks):
-                side_hbm.wait_event(stored[min(i + lag, n_chunks - 1)])
-                c_ops.multi_layer_kv_transfer(hbm_objs[i], ptrs, dev_chunks[i], dev, pbs, False,
+        # Issued in the order an engine would issue them: store chunk i, then
+        # the retrieve that chunk i's store releases (chunk i - lag).
+        for i in range(n_chunks + lag):
+            if i < n_chunks:
+                c_ops.multi_layer_kv_transfer(hbm_objs[i], ptrs, dev_chunks[i], dev, pbs, True,
                                               spec.use_mla)
+            j = i - lag
+            if j >= 0:
+                # chunk j waits for the stores issued so far: through chunk
+                # min(j + lag, last)
+                side_hbm.wait_stream(cap)
+                with torch.cuda.stream(side_hbm):
+                    c_ops.multi_layer_kv_transfer(hbm_objs[j], ptrs, dev_chunks[j], dev, pbs,
+                                                  False, spec.use_mla)
         cap.wait_stream(side_hbm)
     for _ in range(args.warmup):
         g2.replay()
@@ -499,19 +501,20 @@ def run_ours(args):
         """The same calls with the retrieves on a second stream, each chunk's
         retrieve ordered after its store: PCIe carries the stores' writes
         and the retrieves' reads at the same time (full duplex)."""
-        stored = []
-        for i in range(n_chunks):
-            slot_dev_bufs[i].copy_(host_chunks[i], non_blocking=True)
-            c_ops.multi_layer_kv_transfer(host_objs[i], ptrs, slot_dev_bufs[i], dev, pbs, True,
-                                          spec.use_mla)
-            ev = torch.cuda.Event()
-            ev.record(stream)
-            stored.append(ev)
-        with torch.cuda.stream(side):
-            for i in range(n_chunks):
-                side.wait_event(stored[min(i + RETRIEVE_LAG, n_chunks - 1)])
+        lag = min(RETRIEVE_LAG, n_chunks - 1)
+        # Issued in engine order: store chunk i, then the retrieve of chunk
+        # i - lag, which waits for the stores issued so far.
+        for i in range(n_chunks + lag):
+            if i < n_chunks:
+                slot_dev_bufs[i].copy_(host_chunks[i], non_blocking=True)
                 c_ops.multi_layer_kv_transfer(host_objs[i], ptrs, slot_dev_bufs[i], dev, pbs,
-                                              False, spec.use_mla)
+                                              True, spec.use_mla)
+            j = i - lag
+            if j >= 0:
+                side.wait_stream(stream)
+                with torch.cuda.stream(side):
+                    c_ops.multi_layer_kv_transfer(host_objs[j], ptrs, slot_dev_bufs[j], dev, pbs,
+                                                  False, spec.use_mla)
         stream.wait_stream(side)
 
     e2e_steps = args.e2e_steps or args.steps

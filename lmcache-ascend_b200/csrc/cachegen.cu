@@ -146,36 +146,72 @@ __device__ __forceinline__ void load_cdf_rows(uint32_t* s_cdf, const uint16_t* c
   for (int k = 0; k <= max_bins; ++k) s_cdf[k * kCoderThreads + threadIdx.x] = row[k];
 }
 
-struct ByteSink {
+// The bytes of one encoded stream, appended in order. With kWords (4-byte
+// aligned stream start and capacity) they collect in a 64-bit accumulator and
+// leave as whole 32-bit words; otherwise they are stored one by one. Bytes at
+// positions >= cap are dropped and set `overflow`.
+template <bool kWords>
+struct StreamSink {
   uint8_t* out;
   int64_t cap;
-  int64_t pos;
-  uint32_t word;
-  bool words;  // 4-byte aligned stream start and cap % 4 == 0
+  int64_t pos;   // !kWords: bytes appended
+  int64_t done;  // kWords: whole words written (or dropped)
+  uint64_t acc;  // kWords: pending bytes, the oldest in the low byte
+  int na;        // kWords: bytes pending in acc, 0..3 between appends
   bool overflow;
 
-  __device__ __forceinline__ void put(uint32_t b) {
-    b &= 0xffu;
-    if (pos < cap) {
-      if (words) {
-        word |= b << (8 * (pos & 3));
-        if ((pos & 3) == 3) {
-          reinterpret_cast<uint32_t*>(out)[pos >> 2] = word;
-          word = 0;
-        }
-      } else {
-        out[pos] = static_cast<uint8_t>(b);
-      }
-    } else {
-      overflow = true;
-    }
-    ++pos;
+  __device__ __forceinline__ void init(uint8_t* o, int64_t c) {
+    out = o;
+    cap = c;
+    pos = 0;
+    done = 0;
+    acc = 0;
+    na = 0;
+    overflow = false;
   }
 
-  __device__ __forceinline__ void flush() {
-    if (words && (pos & 3) != 0 && pos <= cap) {
-      const int64_t base = pos & ~int64_t(3);
-      for (int64_t i = base; i < pos; ++i) out[i] = static_cast<uint8_t>(word >> (8 * (i - base)));
+  // Appends the k (0..4) bytes in the low bytes of v, the first in the
+  // lowest byte; the bytes of v above them are zero.
+  __device__ __forceinline__ void append(uint32_t v, int k) {
+    if constexpr (kWords) {
+      acc |= static_cast<uint64_t>(v) << (8 * na);
+      na += k;
+      if (na >= 4) {
+        if (done < (cap >> 2)) {
+          reinterpret_cast<uint32_t*>(out)[done] = static_cast<uint32_t>(acc);
+        } else {
+          overflow = true;
+        }
+        ++done;
+        acc >>= 32;
+        na -= 4;
+      }
+    } else {
+      for (int i = 0; i < k; ++i) {
+        if (pos + i < cap) {
+          out[pos + i] = static_cast<uint8_t>(v >> (8 * i));
+        } else {
+          overflow = true;
+        }
+      }
+      pos += k;
+    }
+  }
+
+  // Writes the pending bytes; returns the stream length.
+  __device__ __forceinline__ int64_t finish() {
+    if constexpr (kWords) {
+      const int64_t base = done * 4;
+      if (na > 0) {
+        if (base < cap) {  // cap % 4 == 0, so all na bytes fit
+          for (int i = 0; i < na; ++i) out[base + i] = static_cast<uint8_t>(acc >> (8 * i));
+        } else {
+          overflow = true;
+        }
+      }
+      return base + na;
+    } else {
+      return pos;
     }
   }
 };
@@ -184,6 +220,7 @@ struct ByteSink {
 // straight from global memory (a warp reads one 32-byte run of a token row)
 // kSymAhead tokens ahead of their use, so their latency overlaps the coding
 // of the tokens before them; no block-wide barrier after the CDF load.
+template <bool kWords>
 __global__ void __launch_bounds__(kCoderThreads)
 encode_kernel(const uint16_t* __restrict__ cdf, const uint8_t* __restrict__ sym,
               uint8_t* __restrict__ out, int32_t* __restrict__ lengths, int T, int C,
@@ -200,13 +237,8 @@ encode_kernel(const uint16_t* __restrict__ cdf, const uint8_t* __restrict__ sym,
 
   const uint32_t* my_cdf = s_cdf + tid;  // my_cdf[k * kCoderThreads] = cdf[k]
   const int64_t stream = static_cast<int64_t>(l) * C + c;
-  ByteSink sink;
-  sink.out = out + stream * stride;
-  sink.cap = stride;
-  sink.pos = 0;
-  sink.word = 0;
-  sink.words = ((reinterpret_cast<uintptr_t>(out) | static_cast<uint64_t>(stride)) & 3) == 0;
-  sink.overflow = false;
+  StreamSink<kWords> sink;
+  sink.init(out + stream * stride, stride);
   uint32_t low = 0, range = 0xFFFFFFFFu;
   bool oor = false;
   const uint8_t* in = sym + static_cast<int64_t>(l) * T * C + c;
@@ -221,16 +253,32 @@ encode_kernel(const uint16_t* __restrict__ cdf, const uint8_t* __restrict__ sym,
     const uint32_t r = range >> kProbBits;
     low += lo * r;
     range = r * (hi - lo);
-    // At most four byte shifts are ever needed; the bound only guards
+    // Renormalisation emits the top byte of low while it is settled (the
+    // same in low and low + range). A shift by 8 bits shifts d = low ^
+    // (low + range) by 8 bits too, so the settled bytes are d's leading zero
+    // bytes: k = clz(d) / 8 <= 3 of them leave at once, with no loop.
+    const uint32_t d = low ^ (low + range);
+    const int k = d != 0 ? static_cast<int>(__clz(d) >> 3) : 0;
+    if (k > 0) {
+      const uint32_t rev = __byte_perm(low, 0, 0x0123);  // top byte of low lowest
+      sink.append(rev & ((1u << (8 * k)) - 1u), k);
+      low <<= 8 * k;
+      range <<= 8 * k;
+    }
+    // Now the top byte is unsettled. Done if range >= BOT. Otherwise (or for
+    // d == 0, which a valid CDF never produces) continue with the step-by-step
+    // rule; at most a few more shifts ever happen, and the bound only guards
     // against a state the coder cannot reach.
-    for (int it = 0; it < kMaxRenorm; ++it) {
-      if ((low ^ (low + range)) >= kTop) {
-        if (range >= kBot) break;
-        range = (0u - low) & (kBot - 1u);
+    if (range < kBot || d == 0) {
+      for (int it = k; it < kMaxRenorm; ++it) {
+        if ((low ^ (low + range)) >= kTop) {
+          if (range >= kBot) break;
+          range = (0u - low) & (kBot - 1u);
+        }
+        sink.append(low >> 24, 1);
+        low <<= 8;
+        range <<= 8;
       }
-      sink.put(low >> 24);
-      low <<= 8;
-      range <<= 8;
     }
   };
 
@@ -259,12 +307,10 @@ encode_kernel(const uint16_t* __restrict__ cdf, const uint8_t* __restrict__ sym,
   for (int j = 0; j < kSymAhead; ++j) {
     if (t0 + j < T) code_symbol(cur[j]);
   }
-  for (int i = 0; i < 4; ++i) {
-    sink.put(low >> 24);
-    low <<= 8;
-  }
-  sink.flush();
-  lengths[stream] = sink.overflow ? -1 : static_cast<int32_t>(sink.pos);
+  // Four bytes of low end the stream.
+  sink.append(__byte_perm(low, 0, 0x0123), 4);
+  const int64_t n = sink.finish();
+  lengths[stream] = sink.overflow ? -1 : static_cast<int32_t>(n);
   if (sink.overflow) raise_flag(status, LMCB_DEVICE_FLAG_STREAM_OVERFLOW);
   if (oor) raise_flag(status, LMCB_DEVICE_FLAG_SYMBOL_OUT_OF_RANGE);
 }
@@ -531,11 +577,21 @@ int lmcb_encode(const int16_t* cdf, const int8_t* inputSym, uint8_t* outputBuffe
   unsigned int* status = lmcb::device_status_ptr();
   if (status == nullptr) return LMCB_ERR_CUDA;
   const size_t smem = lmcb::coder_smem_bytes(maxBins);
-  LMCB_CUDA_TRY(lmcb::ensure_smem_limit<&lmcb::encode_kernel>(smem, lmcb::coder_smem_cap()));
   dim3 grid((numChannels + lmcb::kCoderThreads - 1) / lmcb::kCoderThreads, numLayers);
-  lmcb::encode_kernel<<<grid, lmcb::kCoderThreads, smem, static_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const uint16_t*>(cdf), reinterpret_cast<const uint8_t*>(inputSym),
-      outputBuffer, outputLengths, numTokens, numChannels, maxBins, bufferStride, status);
+  const bool words =
+      ((reinterpret_cast<uintptr_t>(outputBuffer) | static_cast<uint64_t>(bufferStride)) & 3) == 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (words) {
+    LMCB_CUDA_TRY(lmcb::ensure_smem_limit<&lmcb::encode_kernel<true>>(smem, lmcb::coder_smem_cap()));
+    lmcb::encode_kernel<true><<<grid, lmcb::kCoderThreads, smem, s>>>(
+        reinterpret_cast<const uint16_t*>(cdf), reinterpret_cast<const uint8_t*>(inputSym),
+        outputBuffer, outputLengths, numTokens, numChannels, maxBins, bufferStride, status);
+  } else {
+    LMCB_CUDA_TRY(lmcb::ensure_smem_limit<&lmcb::encode_kernel<false>>(smem, lmcb::coder_smem_cap()));
+    lmcb::encode_kernel<false><<<grid, lmcb::kCoderThreads, smem, s>>>(
+        reinterpret_cast<const uint16_t*>(cdf), reinterpret_cast<const uint8_t*>(inputSym),
+        outputBuffer, outputLengths, numTokens, numChannels, maxBins, bufferStride, status);
+  }
   LMCB_CUDA_TRY(cudaGetLastError());
   return LMCB_OK;
 }
