@@ -350,10 +350,6 @@ __device__ __forceinline__ void bulk_wait_reads_done() {
 }
 
 constexpr int kBatchRows = 256;   // rows resolved together (8 per lane)
-// The first batch after griddepcontrol.wait is one row per lane, so the first
-// bulk loads issue after one slot-load latency and little address arithmetic;
-// later batches are resolved while earlier groups are in flight.
-constexpr int kFirstBatchRows = 32;
 // Bit 63 of a resolved destination marks a row that is not 16-byte aligned
 // (user-space addresses never set it).
 constexpr uint64_t kMisalignedTag = uint64_t(1) << 63;
@@ -384,10 +380,16 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b) {
   const int32_t r_end = static_cast<int32_t>(static_cast<int64_t>(b.num_rows) * (blockIdx.x + 1) / gridDim.x);
   const int32_t n_rows = r_end - r_begin;
   const uint32_t row_bytes = static_cast<uint32_t>(p.row_bytes);
-  // Batches: kFirstBatchRows rows, then kBatchRows rows each. Groups never
-  // straddle a batch: a batch of n rows holds ceil(n / stage_rows) groups.
+  // Batches: first_batch rows, then kBatchRows rows each. The first batch
+  // after griddepcontrol.wait is what the ring takes at once (stages x
+  // stage_rows, at most kBatchRows): the first loads issue after one
+  // slot-load latency and no more address arithmetic than they need, and a
+  // CTA with few rows resolves them all in that one latency. Later batches are
+  // resolved while earlier groups are in flight. Groups never straddle a
+  // batch: a batch of n rows holds ceil(n / stage_rows) groups.
   const int32_t groups_per_batch = (kBatchRows + b.stage_rows - 1) / b.stage_rows;
-  const int32_t first_rows = min(kFirstBatchRows, n_rows);
+  const int32_t first_batch = min(kBatchRows, b.stages * b.stage_rows);
+  const int32_t first_rows = min(first_batch, n_rows);
   const int32_t rest_rows = n_rows - first_rows;
   const int32_t full_batches = rest_rows / kBatchRows;
   const int32_t tail_rows = rest_rows - full_batches * kBatchRows;
@@ -469,7 +471,7 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b) {
   auto issue_load = [&](int st) {
     if (cur_next >= cur_n) {
       cur_b0 += cur_n;
-      cur_n = min(cur_b0 == 0 ? kFirstBatchRows : kBatchRows, n_rows - cur_b0);
+      cur_n = min(cur_b0 == 0 ? first_batch : kBatchRows, n_rows - cur_b0);
       cur_next = 0;
       resolve_batch(cur_b0, cur_n);
     }
