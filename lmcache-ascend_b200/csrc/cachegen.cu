@@ -171,21 +171,21 @@ struct StreamSink {
   }
 
   // Appends the k (0..4) bytes in the low bytes of v, the first in the
-  // lowest byte; the bytes of v above them are zero.
+  // lowest byte; the bytes of v above them are zero. In words mode the body
+  // is straight-line (a predicated store, selects): lanes of a warp fill
+  // their words on different steps, so a branch here would be taken by some
+  // lane on almost every step.
   __device__ __forceinline__ void append(uint32_t v, int k) {
     if constexpr (kWords) {
       acc |= static_cast<uint64_t>(v) << (8 * na);
       na += k;
-      if (na >= 4) {
-        if (done < (cap >> 2)) {
-          reinterpret_cast<uint32_t*>(out)[done] = static_cast<uint32_t>(acc);
-        } else {
-          overflow = true;
-        }
-        ++done;
-        acc >>= 32;
-        na -= 4;
-      }
+      const bool full = na >= 4;
+      const bool fits = done < (cap >> 2);
+      if (full && fits) reinterpret_cast<uint32_t*>(out)[done] = static_cast<uint32_t>(acc);
+      overflow |= full && !fits;
+      done += full ? 1 : 0;
+      acc = full ? (acc >> 32) : acc;
+      na -= full ? 4 : 0;
     } else {
       for (int i = 0; i < k; ++i) {
         if (pos + i < cap) {
@@ -259,12 +259,11 @@ encode_kernel(const uint16_t* __restrict__ cdf, const uint8_t* __restrict__ sym,
     // bytes: k = clz(d) / 8 <= 3 of them leave at once, with no loop.
     const uint32_t d = low ^ (low + range);
     const int k = d != 0 ? static_cast<int>(__clz(d) >> 3) : 0;
-    if (k > 0) {
-      const uint32_t rev = __byte_perm(low, 0, 0x0123);  // top byte of low lowest
-      sink.append(rev & ((1u << (8 * k)) - 1u), k);
-      low <<= 8 * k;
-      range <<= 8 * k;
-    }
+    // Straight-line for every k, 0 included (mask 0, shifts by 0).
+    const uint32_t rev = __byte_perm(low, 0, 0x0123);  // top byte of low lowest
+    sink.append(rev & ((1u << (8 * k)) - 1u), k);
+    low <<= 8 * k;
+    range <<= 8 * k;
     // Now the top byte is unsettled. Done if range >= BOT. Otherwise (or for
     // d == 0, which a valid CDF never produces) continue with the step-by-step
     // rule; at most a few more shifts ever happen, and the bound only guards
