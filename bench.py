@@ -26,6 +26,7 @@ the max-over-ranks timing).
   python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2]
   python bench.py --impl reference      # CPU path of the reference semantics
   python bench.py --component cachegen  # CacheGen codec kernels
+  python bench.py --component layerwise  # single_layer_kv_transfer, per chunk vs batched
 """
 
 from __future__ import annotations
@@ -58,8 +59,10 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="c2")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--component", default="transfer", choices=["transfer", "cachegen"],
-                    help="cachegen: time the CacheGen CDF / encode / decode kernels instead")
+    ap.add_argument("--component", default="transfer",
+                    choices=["transfer", "cachegen", "layerwise"],
+                    help="cachegen: time the CacheGen CDF / encode / decode kernels instead; "
+                         "layerwise: time the per-layer single_layer_kv_transfer path")
     ap.add_argument("--e2e-steps", type=int, default=None,
                     help="timed steps of the pinned-host leg (default: --steps)")
     ap.add_argument("--cpu-budget", type=float, default=15.0,
@@ -810,10 +813,117 @@ def run_cachegen(args):
     print(json.dumps(line), flush=True)
 
 
+def run_layerwise(args):
+    """The layerwise connector's path (single_layer_kv_transfer) on the c2
+    workload: every layer of every 256-token chunk stored into, then
+    retrieved from, token-major [T, 2, H] objects in HBM. Two ways to issue
+    it:
+    * per chunk: one single_layer_kv_transfer per (layer, chunk), as the
+      reference's layerwise connector issues them (npu_connector.py:227-252);
+    * batched: one single_layer_kv_transfer_batched per layer over all chunks,
+      as this connector issues them."""
+    from lmcache_b200 import c_ops
+    from lmcache_b200 import workloads as wl
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    spec = wl.SPECS[args.workload]
+    if spec.use_mla:
+        raise SystemExit("layerwise: an MLA cache has no separate K and V caches")
+    caches = wl.make_kv_caches(spec, dev, seed=0)
+    slots = wl.make_slot_mapping(spec, seed=0)
+    chunks = [c.to(dev) for c in wl.chunks(slots, spec.chunk_size)]
+    slots_dev = slots.to(dev)
+    bounds = [0]
+    for c in chunks:
+        bounds.append(bounds[-1] + len(c))
+    H = spec.hidden
+    objs = [[torch.empty((len(c), spec.kv, H), dtype=torch.bfloat16, device=dev) for c in chunks]
+            for _ in range(spec.num_layers)]
+    kv_of = [(t[0], t[1]) for t in caches]
+
+    def per_chunk(direction):
+        for layer in range(spec.num_layers):
+            k, v = kv_of[layer]
+            for i, c in enumerate(chunks):
+                c_ops.single_layer_kv_transfer(objs[layer][i], k, v, c, direction, True)
+
+    def batched(direction):
+        for layer in range(spec.num_layers):
+            k, v = kv_of[layer]
+            c_ops.single_layer_kv_transfer_batched(objs[layer], k, v, slots_dev, bounds[:-1],
+                                                   bounds[1:], direction, True)
+
+    payload = wl.payload_bytes(spec, slots)  # one direction
+    n_valid = int((slots >= 0).sum())
+    alg = 2 * (2 * payload + n_valid * 8 * spec.num_layers)  # both directions, HBM bytes
+    peak = measured_peaks()["hbm_gbs"]
+    stream = torch.cuda.current_stream()
+    out = {}
+    # The per-chunk calls are replayed from CUDA graphs (their GPU cost; from
+    # Python they are host-bound at ~5 us a call). The batched calls copy a
+    # per-call object table from host memory, which stream capture refuses,
+    # so they are issued eagerly: 32-80 calls a step, each longer than its
+    # host time.
+    for name, fn, launches in (("per_chunk", per_chunk, spec.num_layers * len(chunks)),
+                               ("batched", batched, spec.num_layers)):
+        for _ in range(args.warmup):
+            fn(True)
+            fn(False)
+        torch.cuda.synchronize()
+        graphs = []
+        if name == "per_chunk":
+            for direction in (True, False):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, capture_error_mode="thread_local"):
+                    fn(direction)
+                graphs.append(g)
+            for _ in range(args.warmup):
+                for g in graphs:
+                    g.replay()
+            run_step = [g.replay for g in graphs]
+        else:
+            run_step = [lambda: fn(True), lambda: fn(False)]
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            for run in run_step:
+                run()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        for g in graphs:
+            g.reset()
+        out[name] = {"gbs": round(2 * payload / (ms / 1e3) / 1e9, 2),
+                     "roofline_frac": round(alg / (ms / 1e3) / 1e9 / peak, 4),
+                     "ms_per_step": round(ms, 4), "launches_per_step": 2 * launches,
+                     "us_per_launch": round(ms * 1e3 / (2 * launches), 2)}
+    line = {
+        "metric": "Layerwise KV store/retrieve GB/s (single_layer_kv_transfer)",
+        "value": out["batched"]["gbs"],
+        "unit": "GB/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "higher_is_better": True,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) bf16 KV, seeded random block slot mappings)",
+        "config": {"workload": f"{args.workload}: every layer of every {spec.chunk_size}-token "
+                               f"chunk, token-major [T, 2, H] objects in HBM, store then "
+                               f"retrieve", "peak_hbm_gbs": peak},
+        "per_chunk": out["per_chunk"],
+        "batched": out["batched"],
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     if args.component == "cachegen":
         run_cachegen(args)
+    elif args.component == "layerwise":
+        run_layerwise(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

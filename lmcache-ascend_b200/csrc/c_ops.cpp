@@ -235,6 +235,19 @@ void multi_layer_kv_transfer(torch::Tensor& key_value,             // [kv, L, T,
       direction ? 1 : 0));
 }
 
+// The batched calls build their object table on the host per call and copy
+// it with cudaMemcpyAsync from a pinned buffer that is released when the call
+// returns. A CUDA graph would keep replaying that copy from the released
+// buffer, so the calls refuse stream capture instead of misbehaving later.
+void reject_capture(cudaStream_t stream, const char* who) {
+  cudaStreamCaptureStatus status = cudaStreamCaptureStatusNone;
+  const cudaError_t err = cudaStreamIsCapturing(stream, &status);
+  TORCH_CHECK(err == cudaSuccess, who, ": ", cudaGetErrorString(err));
+  TORCH_CHECK(status == cudaStreamCaptureStatusNone, who,
+              " cannot be captured in a CUDA graph (its object table is copied from host memory "
+              "each call); issue it outside stream capture");
+}
+
 // All chunks of a request in one launch (an addition to the reference
 // surface; the connector's batched_from_gpu / batched_to_gpu call it).
 // key_values[i] is a [kv, L, T_i, H] object holding slot_mapping[starts[i]:
@@ -289,6 +302,7 @@ void multi_layer_kv_transfer_batched(const std::vector<torch::Tensor>& key_value
   for (const auto& t : key_values) check_device(t, dev, "key_values");
   const c10::OptionalDeviceGuard device_guard(dev);
   cudaStream_t stream = current_stream();
+  reject_capture(stream, "multi_layer_kv_transfer_batched");
   const uint64_t* ptrs = static_cast<const uint64_t*>(get_kernel_ptr(key_value_ptrs));
   const void* slots = get_kernel_ptr(slot_mapping);
   const int64_t esz = first.element_size();
@@ -397,6 +411,7 @@ void single_layer_kv_transfer_batched(const std::vector<torch::Tensor>& lmc_kvs,
   const int slot_dtype = to_slot_dtype(slot_mapping.scalar_type());
   const c10::OptionalDeviceGuard device_guard(dev);
   cudaStream_t stream = current_stream();
+  reject_capture(stream, "single_layer_kv_transfer_batched");
   auto table = torch::empty({3 * n + 1},
                             torch::TensorOptions().dtype(torch::kLong).pinned_memory(true));
   int64_t* tab = table.data_ptr<int64_t>();

@@ -101,19 +101,50 @@ struct TransferParams {
   int32_t obj_token_major;
 };
 
+// A batched launch finds each row's object by a binary search over the token
+// offsets, about log2(num_objects) dependent probes per row. When there are
+// at most kSmemObjects objects the CTA first copies the offsets into shared
+// memory as int32 (token counts are below 2^31), so a probe costs
+// shared-memory latency instead of a dependent global load. Slot starts and
+// object pointers, read once per row, stay in global memory. 1 KB fits beside
+// every ring geometry without costing a CTA per SM.
+constexpr int kSmemObjects = 255;
+
+// Copies the offsets into `s` (kSmemObjects + 1 int32) when they fit and
+// returns the copy, else nullptr; the caller synchronises the CTA before use.
+__device__ __forceinline__ const int32_t* stage_obj_offsets(const TransferParams& p, int32_t* s,
+                                                            int tid, int nthreads) {
+  const int n = p.num_objects;
+  if (n > kSmemObjects) return nullptr;
+  for (int i = tid; i <= n; i += nthreads) s[i] = static_cast<int32_t>(p.obj_offsets[i]);
+  return s;
+}
+
 // LMCache-side row address of (kv, layer, t) and the index of t's slot id.
+// s_offsets: the staged token offsets of a batched launch, or nullptr.
 template <int MODE>
-__device__ __forceinline__ uint8_t* lmc_row(const TransferParams& p, int kv, int layer, int t,
-                                            int64_t* slot_index) {
+__device__ __forceinline__ uint8_t* lmc_row(const TransferParams& p, const int32_t* s_offsets,
+                                            int kv, int layer, int t, int64_t* slot_index) {
   if (batched_mode(MODE)) {
     // Last object whose first token is <= t (empty objects are skipped over).
-    int lo = 0, hi = p.num_objects;  // obj_offsets[lo] <= t < obj_offsets[hi]
-    while (hi - lo > 1) {
-      const int mid = (lo + hi) >> 1;
-      if (__ldg(p.obj_offsets + mid) <= t) lo = mid; else hi = mid;
+    int lo = 0, hi = p.num_objects;  // offsets[lo] <= t < offsets[hi]
+    int64_t first, next;
+    if (s_offsets != nullptr) {
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (s_offsets[mid] <= t) lo = mid; else hi = mid;
+      }
+      first = s_offsets[lo];
+      next = s_offsets[lo + 1];
+    } else {
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (__ldg(p.obj_offsets + mid) <= t) lo = mid; else hi = mid;
+      }
+      first = __ldg(p.obj_offsets + lo);
+      next = __ldg(p.obj_offsets + lo + 1);
     }
-    const int64_t first = __ldg(p.obj_offsets + lo);
-    const int64_t count = __ldg(p.obj_offsets + lo + 1) - first;
+    const int64_t count = next - first;
     const int64_t j = t - first;
     *slot_index = __ldg(p.obj_slot_starts + lo) + j;
     const int64_t row = p.obj_token_major
@@ -152,6 +183,7 @@ transfer_rows_kernel(const TransferParams p) {
   __shared__ const uint8_t* s_src[kMaxTileRows];
   __shared__ uint8_t* s_dst[kMaxTileRows];
   __shared__ int s_warp_count[kMaxTileRows / 32];
+  __shared__ int32_t s_objoff[batched_mode(MODE) ? kSmemObjects + 1 : 1];
 
   const SlotT* __restrict__ slots = static_cast<const SlotT*>(p.slots);
   const int tid = threadIdx.x;
@@ -159,6 +191,11 @@ transfer_rows_kernel(const TransferParams p) {
   const int warp = tid >> 5;
   pdl_wait();
   pdl_launch_dependents();
+  const int32_t* obj_offsets = nullptr;
+  if constexpr (batched_mode(MODE)) {
+    obj_offsets = stage_obj_offsets(p, s_objoff, tid, kThreads);
+    __syncthreads();
+  }
 
   for (int64_t tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
     // tile -> (kv, layer, token range); token tiles vary fastest so
@@ -179,7 +216,7 @@ transfer_rows_kernel(const TransferParams p) {
     if (tid < n_tile) {
       const int t = t0 + tid;
       int64_t slot_index;
-      uint8_t* lmc = lmc_row<MODE>(p, kv, layer, t, &slot_index);
+      uint8_t* lmc = lmc_row<MODE>(p, obj_offsets, kv, layer, t, &slot_index);
       const int64_t slot = static_cast<int64_t>(slots[slot_index]);
       valid = slot >= 0;
       if (valid && p.num_paged_rows > 0 && slot >= p.num_paged_rows) {
@@ -373,6 +410,7 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b) {
   uint64_t* tab_src = s_dst + kBulkMaxStages * 32;      // [kBatchRows] resolved sources
   uint64_t* tab_dst = tab_src + kBatchRows;             // [kBatchRows] resolved destinations
   uint32_t* s_len = reinterpret_cast<uint32_t*>(tab_dst + kBatchRows);  // [kBulkMaxStages][32]
+  int32_t* s_objoff = reinterpret_cast<int32_t*>(s_len + kBulkMaxStages * 32);  // batched only
 
   const int lane = threadIdx.x;
   const SlotT* __restrict__ slots = static_cast<const SlotT*>(p.slots);
@@ -403,6 +441,10 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b) {
   }
   __syncwarp();
 
+  // Batched modes search their object table's token offsets; they are staged
+  // in shared memory right after griddepcontrol.wait (they are an input).
+  const int32_t* obj_offsets = nullptr;
+
   // Resolves rows [b0, b0 + n) of this CTA's range into tab_src / tab_dst
   // (0 for skipped rows). All slot ids and layer bases of the batch are
   // loaded before any is used, so the batch costs one memory latency.
@@ -424,7 +466,7 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b) {
         const int kv = static_cast<int>(b.div_layers.div(q));
         const int layer = static_cast<int>(q - kv * b.div_layers.d);
         int64_t slot_index;
-        lmcs[j] = lmc_row<MODE>(p, kv, layer, tok, &slot_index);
+        lmcs[j] = lmc_row<MODE>(p, obj_offsets, kv, layer, tok, &slot_index);
         slot[j] = static_cast<int64_t>(slots[slot_index]);
         if (!paged_direct(MODE)) {
           const uint64_t* arr = kv == 0 ? p.ptrs_k : p.ptrs_v;
@@ -543,6 +585,10 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b) {
   }
   pdl_wait();
   pdl_launch_dependents();
+  if constexpr (batched_mode(MODE)) {
+    obj_offsets = stage_obj_offsets(p, s_objoff, lane, 32);
+    __syncwarp();
+  }
 
   int64_t issued = 0;
   for (; issued < n_groups && issued < b.stages; ++issued) issue_load(static_cast<int>(issued));
@@ -621,10 +667,10 @@ BulkConfig bulk_config(int64_t row_bytes) {
   return c;
 }
 
-size_t bulk_smem_bytes(const BulkParams& b) {
+size_t bulk_smem_bytes(const BulkParams& b, bool batched) {
   return static_cast<size_t>(b.stages) * b.stage_bytes + kBulkMaxStages * sizeof(uint64_t) +
          kBulkMaxStages * 32 * (sizeof(uint64_t) + sizeof(uint32_t)) +
-         2 * kBatchRows * sizeof(uint64_t);
+         2 * kBatchRows * sizeof(uint64_t) + (batched ? (kSmemObjects + 1) * sizeof(int32_t) : 0);
 }
 
 // LMCB_PDL=0 launches without the programmatic-serialization attribute.
@@ -652,7 +698,7 @@ cudaError_t launch_ex(Kernel* kernel, dim3 grid, dim3 block, size_t smem, cudaSt
 template <typename SlotT, int MODE>
 cudaError_t launch_bulk_mode(const TransferParams& p, const BulkParams& b, int grid,
                              cudaStream_t stream) {
-  const size_t smem = bulk_smem_bytes(b);
+  const size_t smem = bulk_smem_bytes(b, batched_mode(MODE));
   cudaError_t err = ensure_smem_limit<&transfer_rows_bulk_kernel<SlotT, MODE>>(smem, kBulkSmemCap);
   if (err != cudaSuccess) return err;
   return launch_ex(&transfer_rows_bulk_kernel<SlotT, MODE>, dim3(grid), dim3(32), smem, stream,

@@ -177,3 +177,63 @@ def test_single_layer_batched_matches_oracle(token_major, where, transfer_path, 
     for mo in handles:
         arena.free(mo)
     assert c_ops.device_status(torch.cuda.current_device()) == 0
+
+
+def test_many_objects_use_the_global_table(transfer_path):
+    """More objects than the kernels stage in shared memory (255): the object
+    search falls back to the global table."""
+    spec = wl.SPECS["c1"]
+    kv = wl.make_kv_caches(spec, DEV, seed=46)
+    g = torch.Generator().manual_seed(47)
+    slots = torch.randperm(spec.page_buffer_size, generator=g)[:900].to(torch.int64)
+    sd = slots.to(DEV)
+    ptrs = wl.pointer_tensor(kv, DEV)
+    pbs = spec.page_buffer_size
+    ranges = [(3 * i, 3 * i + 3) for i in range(300)]  # 300 objects of 3 tokens
+    ranges[7] = (21, 21)  # an empty one among them
+    objs = [torch.zeros(spec.memobj_shape(e - s), dtype=torch.bfloat16, device=DEV)
+            for s, e in ranges]
+    c_ops.multi_layer_kv_transfer_batched(objs, ptrs, sd, [s for s, _ in ranges],
+                                          [e for _, e in ranges], kv[0].device, pbs, True, False)
+    torch.cuda.synchronize()
+    kv_np = [bits(t) for t in kv]
+    for obj, (s, e) in zip(objs, ranges):
+        want = np.zeros(obj.shape, dtype=np.int16)
+        oracle.multi_layer_kv_transfer(want, kv_np, slots[s:e].numpy(), pbs, True, False)
+        assert np.array_equal(bits(obj), want)
+    kv_new = [torch.zeros_like(t) for t in kv]
+    c_ops.multi_layer_kv_transfer_batched(objs, wl.pointer_tensor(kv_new, DEV), sd,
+                                          [s for s, _ in ranges], [e for _, e in ranges],
+                                          kv[0].device, pbs, False, False)
+    torch.cuda.synchronize()
+    new_np = [np.zeros_like(a) for a in kv_np]
+    for obj, (s, e) in zip(objs, ranges):
+        oracle.multi_layer_kv_transfer(bits(obj), new_np, slots[s:e].numpy(), pbs, False, False)
+    for a, b in zip(kv_new, new_np):
+        assert np.array_equal(bits(a), b)
+
+
+def test_batched_refuses_stream_capture():
+    """The batched calls copy a per-call object table from host memory, so
+    they raise under CUDA graph capture instead of recording that copy."""
+    spec = wl.SPECS["c1"]
+    kv = wl.make_kv_caches(spec, DEV, seed=48)
+    sd = wl.make_slot_mapping(spec, seed=48).to(DEV)
+    objs = [torch.zeros(spec.memobj_shape(128), dtype=torch.bfloat16, device=DEV)
+            for _ in range(2)]
+    ptrs = wl.pointer_tensor(kv, DEV)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with pytest.raises(RuntimeError, match="cannot be captured"):
+        with torch.cuda.graph(graph):
+            c_ops.multi_layer_kv_transfer_batched(objs, ptrs, sd, [0, 128], [128, 256],
+                                                  kv[0].device, spec.page_buffer_size, True,
+                                                  False)
+    k = kv[0][0]
+    v = kv[0][1]
+    lmc = [torch.zeros((128, 2, spec.hidden), dtype=torch.bfloat16, device=DEV) for _ in range(2)]
+    graph2 = torch.cuda.CUDAGraph()
+    with pytest.raises(RuntimeError, match="cannot be captured"):
+        with torch.cuda.graph(graph2):
+            c_ops.single_layer_kv_transfer_batched(lmc, k, v, sd, [0, 128], [128, 256], True,
+                                                   True)
