@@ -135,8 +135,9 @@ LMCB_API int lmcb_multi_layer_kv_transfer_unilateral_kernel(
  * that of lmcb_multi_layer_kv_transfer_kernel on each object in turn.
  *   objectPtrs, tokenOffsets ([numObjects + 1], ascending, tokenOffsets[0]
  *   = 0, tokenOffsets[numObjects] = totalTokens), slotStarts: device-readable
- *   objectsOnDevice  1 if every object is device memory (bulk-copy path),
- *                    0 if any is host memory (zero-copy path) */
+ *   until the launch completes (the kernel reads them)
+ *   objectsOnDevice  1 if every object is device memory (the bulk-copy kernel
+ *                    may then be chosen), 0 if any is host memory (zero-copy) */
 LMCB_API int lmcb_multi_layer_kv_transfer_batched_kernel(
     int type, int slotType, void* stream, const uint64_t* pagedKVCaches,
     const uint64_t* objectPtrs, const int64_t* tokenOffsets, const int64_t* slotStarts,

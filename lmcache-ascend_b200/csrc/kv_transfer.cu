@@ -1,14 +1,23 @@
 // kv_transfer.cu -- paged KV-cache <-> LMCache object row transfer for sm_100a.
 //
-// One kernel core serves every transfer entry point of the reference's c_ops
-// surface (csrc/mem_kernels.cpp): it copies "rows" (one token's hidden_dims
+// Two kernels serve every transfer entry point of the reference's c_ops
+// surface (csrc/mem_kernels.cpp). Both copy "rows" (one token's hidden_dims
 // elements of K, V or the MLA latent) between vLLM-style paged buffers,
-// addressed through slot ids, and a dense LMCache object. The entry points
+// addressed through slot ids, and dense LMCache objects. The entry points
 // only differ in how a (kv, layer, slot) triple becomes a paged-side address
-// and a (kv, layer, token) triple becomes an LMCache-side address.
+// and a (kv, layer, token) triple becomes an LMCache-side address (PagedMode).
 //
-// Work decomposition: a tile is (kv, layer, TILE consecutive tokens). A CTA
-// takes tiles in a grid-stride loop. For each tile it
+//   transfer_rows_bulk_kernel  one-warp CTAs stream contiguous row ranges
+//       through a shared-memory ring with bulk (TMA engine) copies, merging
+//       rows that are contiguous on both sides; device objects only. Used
+//       for launches under kVectorMinTraffic whose copies can merge or whose
+//       rows are at least kBulkMinUnmergedRow bytes (launch_transfer).
+//   transfer_rows_kernel       vectorised loads and stores, below; every
+//       other case, pinned-host (zero-copy) objects included.
+//
+// transfer_rows_kernel's work decomposition: a tile is (kv, layer, TILE
+// consecutive tokens). A CTA takes tiles in a grid-stride loop. For each tile
+// it
 //   1. resolves the tile's rows once: slot id -> paged address, token ->
 //      LMCache address, dropping skipped rows (slot < 0 or out of range) and
 //      compacting the rest into shared memory;
