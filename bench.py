@@ -27,6 +27,7 @@ the max-over-ranks timing).
   python bench.py --impl reference      # CPU path of the reference semantics
   python bench.py --component cachegen  # CacheGen codec kernels
   python bench.py --component layerwise  # single_layer_kv_transfer, per chunk vs batched
+  python bench.py --component rotary     # fused K re-rotation
 """
 
 from __future__ import annotations
@@ -60,9 +61,10 @@ def parse_args():
     ap.add_argument("--workload", default="c2")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--component", default="transfer",
-                    choices=["transfer", "cachegen", "layerwise"],
+                    choices=["transfer", "cachegen", "layerwise", "rotary"],
                     help="cachegen: time the CacheGen CDF / encode / decode kernels instead; "
-                         "layerwise: time the per-layer single_layer_kv_transfer path")
+                         "layerwise: time the per-layer single_layer_kv_transfer path; "
+                         "rotary: time the fused K re-rotation")
     ap.add_argument("--e2e-steps", type=int, default=None,
                     help="timed steps of the pinned-host leg (default: --steps)")
     ap.add_argument("--cpu-budget", type=float, default=15.0,
@@ -918,12 +920,68 @@ def run_layerwise(args):
     print(json.dumps(line), flush=True)
 
 
+def run_rotary(args):
+    """rotary_embedding_k_fused (CacheBlend's K re-rotation) over the cached K
+    of a c2-shaped request: 32 layers x 8192 tokens x 8 heads x 128 bf16 (512
+    MiB, one call over all rows, as the op is per token), moved from positions
+    0..8191 to 4096..12287, neox layout, fp32 cos/sin cache of 32768
+    positions. GB/s of algorithmic HBM bytes (K read and written, two cache
+    rows and two positions per token) against the copy roofline."""
+    from lmcache_b200 import c_ops
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    L, T, heads, hd, max_pos = 32, 8192, 8, 128, 32768
+    g = torch.Generator(device=dev).manual_seed(0)
+    key = torch.randn(L * T, heads, hd, generator=g, device=dev).to(torch.bfloat16)
+    old = torch.arange(T, device=dev, dtype=torch.int64).repeat(L)
+    new = old + 4096
+    inv = 1.0 / (10000.0 ** (torch.arange(0, hd, 2, dtype=torch.float64) / hd))
+    freqs = torch.outer(torch.arange(max_pos, dtype=torch.float64), inv)
+    cache = torch.cat([freqs.cos(), freqs.sin()], dim=-1).to(torch.float32).to(dev)
+    n = L * T
+    alg = 2 * key.numel() * key.element_size() + n * 2 * hd * 4 + n * 2 * 8
+    for _ in range(args.warmup):
+        c_ops.rotary_embedding_k_fused(old, new, key, hd, cache, True)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        c_ops.rotary_embedding_k_fused(old, new, key, hd, cache, True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    peak = measured_peaks()["hbm_gbs"]
+    gbs = alg / (ms / 1e3) / 1e9
+    line = {
+        "metric": "Fused K re-rotation GB/s (rotary_embedding_k_fused)",
+        "value": round(gbs, 2),
+        "unit": "GB/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "higher_is_better": True,
+        "dtype": "bf16 keys, fp32 math",
+        "data": "synthetic (seeded N(0,1) bf16 K)",
+        "config": {"workload": "c2-shaped K: 32 layers x 8192 tokens x 8 heads x 128, neox, "
+                               "positions +4096, fp32 cos/sin cache of 32768 positions",
+                   "algorithmic_bytes": alg},
+        "us_per_call": round(ms * 1e3, 1),
+        "roofline_frac": round(gbs / peak, 4),
+        "peak_hbm_gbs": peak,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     if args.component == "cachegen":
         run_cachegen(args)
     elif args.component == "layerwise":
         run_layerwise(args)
+    elif args.component == "rotary":
+        run_rotary(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

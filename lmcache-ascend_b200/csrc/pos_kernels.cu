@@ -55,43 +55,52 @@ struct RopeParams {
   int64_t max_position;
   int is_neox;
   unsigned int* status;
+  FastDiv div_half;  // pair index -> (head, i): division by rot_dim / 2
 };
 
+// A CTA walks tokens in a grid-stride loop (one launch of up to
+// kRopeBlocksPerSm CTAs per SM, instead of a tiny CTA per token); within a
+// token, thread q handles rotated pairs q, q + blockDim.x, ... with 32-bit
+// pair arithmetic (pairs per token = num_heads * rot_dim / 2 < 2^31, checked
+// by the entry point).
 template <typename KeyT, typename CacheT, typename PosT>
 __global__ void __launch_bounds__(kRopeThreads) rope_k_fused_kernel(const RopeParams p) {
-  const int64_t token = blockIdx.x;
-  if (token >= p.num_tokens) return;
-  const int64_t a = static_cast<int64_t>(static_cast<const PosT*>(p.old_pos)[token]);
-  const int64_t b = static_cast<int64_t>(static_cast<const PosT*>(p.new_pos)[token]);
-  if (a < 0 || a >= p.max_position || b < 0 || b >= p.max_position) {
-    if (threadIdx.x == 0) raise_flag(p.status, LMCB_DEVICE_FLAG_POSITION_OUT_OF_RANGE);
-    return;
-  }
-  const int64_t half = p.rot_dim / 2;
-  const CacheT* ca = static_cast<const CacheT*>(p.cache) + a * p.rot_dim;
-  const CacheT* cb = static_cast<const CacheT*>(p.cache) + b * p.rot_dim;
-  KeyT* k = static_cast<KeyT*>(p.key) + token * p.token_stride;
-  const int64_t pairs = p.num_heads * half;
-  for (int64_t q = threadIdx.x; q < pairs; q += blockDim.x) {
-    const int64_t h = q / half;
-    const int64_t i = q - h * half;
-    const float cos_a = to_f(ca[i]), sin_a = to_f(ca[half + i]);
-    const float cos_b = to_f(cb[i]), sin_b = to_f(cb[half + i]);
-    const float c = cos_b * cos_a + sin_b * sin_a;
-    const float s = sin_b * cos_a - cos_b * sin_a;
-    KeyT* row = k + h * p.head_size;
-    const int64_t i1 = p.is_neox ? i : 2 * i;
-    const int64_t i2 = p.is_neox ? i + half : 2 * i + 1;
-    const float x1 = to_f(row[i1]);
-    const float x2 = to_f(row[i2]);
-    row[i1] = from_f<KeyT>(x1 * c - x2 * s);
-    row[i2] = from_f<KeyT>(x2 * c + x1 * s);
+  const int half = static_cast<int>(p.rot_dim / 2);
+  const int pairs = static_cast<int>(p.num_heads) * half;
+  for (int64_t token = blockIdx.x; token < p.num_tokens; token += gridDim.x) {
+    const int64_t a = static_cast<int64_t>(static_cast<const PosT*>(p.old_pos)[token]);
+    const int64_t b = static_cast<int64_t>(static_cast<const PosT*>(p.new_pos)[token]);
+    if (a < 0 || a >= p.max_position || b < 0 || b >= p.max_position) {
+      if (threadIdx.x == 0) raise_flag(p.status, LMCB_DEVICE_FLAG_POSITION_OUT_OF_RANGE);
+      continue;  // uniform across the CTA
+    }
+    const CacheT* ca = static_cast<const CacheT*>(p.cache) + a * p.rot_dim;
+    const CacheT* cb = static_cast<const CacheT*>(p.cache) + b * p.rot_dim;
+    KeyT* k = static_cast<KeyT*>(p.key) + token * p.token_stride;
+    for (int q = threadIdx.x; q < pairs; q += blockDim.x) {
+      const int h = static_cast<int>(p.div_half.div(static_cast<uint32_t>(q)));
+      const int i = q - h * half;
+      const float cos_a = to_f(ca[i]), sin_a = to_f(ca[half + i]);
+      const float cos_b = to_f(cb[i]), sin_b = to_f(cb[half + i]);
+      const float c = cos_b * cos_a + sin_b * sin_a;
+      const float s = sin_b * cos_a - cos_b * sin_a;
+      KeyT* row = k + static_cast<int64_t>(h) * p.head_size;
+      const int i1 = p.is_neox ? i : 2 * i;
+      const int i2 = p.is_neox ? i + half : 2 * i + 1;
+      const float x1 = to_f(row[i1]);
+      const float x2 = to_f(row[i2]);
+      row[i1] = from_f<KeyT>(x1 * c - x2 * s);
+      row[i2] = from_f<KeyT>(x2 * c + x1 * s);
+    }
   }
 }
 
+constexpr int kRopeBlocksPerSm = 16;
+
 template <typename KeyT, typename CacheT>
 cudaError_t launch_rope_pos(const RopeParams& p, int pos_type, cudaStream_t stream) {
-  const dim3 grid(static_cast<unsigned>(p.num_tokens));
+  const int64_t max_grid = static_cast<int64_t>(current_sm_count()) * kRopeBlocksPerSm;
+  const dim3 grid(static_cast<unsigned>(p.num_tokens < max_grid ? p.num_tokens : max_grid));
   if (pos_type == LMCB_DTYPE_INT64) {
     rope_k_fused_kernel<KeyT, CacheT, int64_t><<<grid, kRopeThreads, 0, stream>>>(p);
   } else {
@@ -135,7 +144,7 @@ int lmcb_rotary_embedding_k_fused(const void* oldPositions, const void* newPosit
   }
   if (numTokens < 0 || numHeads < 0 || headSize <= 0 || rotDim <= 0 || rotDim % 2 != 0 ||
       rotDim > headSize || maxPosition <= 0 || keyTokenStride < numHeads * headSize ||
-      numTokens > 0x7fffffff) {
+      numTokens > 0x7fffffff || numHeads * (rotDim / 2) > 0x7fffffff) {
     return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT,
                       std::string(who) + ": invalid shape (rot_dim must be even and <= head_size).");
   }
@@ -156,6 +165,7 @@ int lmcb_rotary_embedding_k_fused(const void* oldPositions, const void* newPosit
   p.rot_dim = rotDim;
   p.max_position = maxPosition;
   p.is_neox = isNeox ? 1 : 0;
+  p.div_half = lmcb::FastDiv(static_cast<uint32_t>(rotDim / 2));
   p.status = lmcb::device_status_ptr();
   if (p.status == nullptr) return LMCB_ERR_CUDA;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
