@@ -55,7 +55,7 @@ struct RopeParams {
   int64_t max_position;
   int is_neox;
   unsigned int* status;
-  FastDiv div_half;  // pair index -> (head, i): division by rot_dim / 2
+  FastDiv div_half;  // pair index -> head: by rot_dim / 2 (rot_dim / 4 in the vec2 kernel)
 };
 
 // A CTA walks tokens in a grid-stride loop (one launch of up to
@@ -95,13 +95,106 @@ __global__ void __launch_bounds__(kRopeThreads) rope_k_fused_kernel(const RopePa
   }
 }
 
+// Same rotation, two adjacent pairs per step with 2-element vector accesses:
+// neox pairs (i, i + half) and (i + 1, i + 1 + half), GPT-J pairs (2i, 2i + 1)
+// and (2i + 2, 2i + 3), i even; cos/sin of both pairs come in one 2-element
+// load each. The per-pair arithmetic is that of rope_k_fused_kernel, so the
+// results are identical. Launched only when the host has checked that every
+// access is aligned to its vector width (rope_vec_ok).
+template <typename T, int N>
+struct alignas(sizeof(T) * N) RopeVec {
+  T v[N];
+};
+
+template <typename KeyT, typename CacheT, typename PosT>
+__global__ void __launch_bounds__(kRopeThreads) rope_k_fused_vec2_kernel(const RopeParams p) {
+  const int half = static_cast<int>(p.rot_dim / 2);
+  const int quads = static_cast<int>(p.num_heads) * (half / 2);  // pair pairs per token
+  const FastDiv& div_q = p.div_half;  // here: division by half / 2
+  for (int64_t token = blockIdx.x; token < p.num_tokens; token += gridDim.x) {
+    const int64_t a = static_cast<int64_t>(static_cast<const PosT*>(p.old_pos)[token]);
+    const int64_t b = static_cast<int64_t>(static_cast<const PosT*>(p.new_pos)[token]);
+    if (a < 0 || a >= p.max_position || b < 0 || b >= p.max_position) {
+      if (threadIdx.x == 0) raise_flag(p.status, LMCB_DEVICE_FLAG_POSITION_OUT_OF_RANGE);
+      continue;  // uniform across the CTA
+    }
+    const CacheT* ca = static_cast<const CacheT*>(p.cache) + a * p.rot_dim;
+    const CacheT* cb = static_cast<const CacheT*>(p.cache) + b * p.rot_dim;
+    KeyT* k = static_cast<KeyT*>(p.key) + token * p.token_stride;
+    for (int q = threadIdx.x; q < quads; q += blockDim.x) {
+      const int h = static_cast<int>(div_q.div(static_cast<uint32_t>(q)));
+      const int i = 2 * (q - h * (half / 2));
+      using C2 = RopeVec<CacheT, 2>;
+      const C2 cos_a = *reinterpret_cast<const C2*>(ca + i);
+      const C2 sin_a = *reinterpret_cast<const C2*>(ca + half + i);
+      const C2 cos_b = *reinterpret_cast<const C2*>(cb + i);
+      const C2 sin_b = *reinterpret_cast<const C2*>(cb + half + i);
+      float c[2], sn[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const float ca_j = to_f(cos_a.v[j]), sa_j = to_f(sin_a.v[j]);
+        const float cb_j = to_f(cos_b.v[j]), sb_j = to_f(sin_b.v[j]);
+        c[j] = cb_j * ca_j + sb_j * sa_j;
+        sn[j] = sb_j * ca_j - cb_j * sa_j;
+      }
+      KeyT* row = k + static_cast<int64_t>(h) * p.head_size;
+      if (p.is_neox) {
+        using K2 = RopeVec<KeyT, 2>;
+        K2* p1 = reinterpret_cast<K2*>(row + i);
+        K2* p2 = reinterpret_cast<K2*>(row + half + i);
+        K2 x1 = *p1, x2 = *p2;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const float v1 = to_f(x1.v[j]), v2 = to_f(x2.v[j]);
+          x1.v[j] = from_f<KeyT>(v1 * c[j] - v2 * sn[j]);
+          x2.v[j] = from_f<KeyT>(v2 * c[j] + v1 * sn[j]);
+        }
+        *p1 = x1;
+        *p2 = x2;
+      } else {
+        using K4 = RopeVec<KeyT, 4>;
+        K4* px = reinterpret_cast<K4*>(row + 2 * i);
+        K4 x = *px;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const float v1 = to_f(x.v[2 * j]), v2 = to_f(x.v[2 * j + 1]);
+          x.v[2 * j] = from_f<KeyT>(v1 * c[j] - v2 * sn[j]);
+          x.v[2 * j + 1] = from_f<KeyT>(v2 * c[j] + v1 * sn[j]);
+        }
+        *px = x;
+      }
+    }
+  }
+}
+
 constexpr int kRopeBlocksPerSm = 16;
 
+// True when every access of rope_k_fused_vec2_kernel is aligned: rot_dim a
+// multiple of 4 (so i and half + i are even), the key base, token stride and
+// head size multiples of the key vector (2 elements neox, 4 GPT-J) and the
+// cache base a multiple of 2 cache elements.
 template <typename KeyT, typename CacheT>
-cudaError_t launch_rope_pos(const RopeParams& p, int pos_type, cudaStream_t stream) {
+bool rope_vec_ok(const RopeParams& p) {
+  if (p.rot_dim % 4 != 0) return false;
+  const int64_t kv = p.is_neox ? 2 : 4;
+  const uint64_t kbytes = static_cast<uint64_t>(kv) * sizeof(KeyT);
+  if (reinterpret_cast<uintptr_t>(p.key) % kbytes != 0) return false;
+  if ((p.token_stride % kv) != 0 || (p.head_size % kv) != 0) return false;
+  return reinterpret_cast<uintptr_t>(p.cache) % (2 * sizeof(CacheT)) == 0;
+}
+
+template <typename KeyT, typename CacheT>
+cudaError_t launch_rope_pos(RopeParams p, int pos_type, cudaStream_t stream) {
   const int64_t max_grid = static_cast<int64_t>(current_sm_count()) * kRopeBlocksPerSm;
   const dim3 grid(static_cast<unsigned>(p.num_tokens < max_grid ? p.num_tokens : max_grid));
-  if (pos_type == LMCB_DTYPE_INT64) {
+  if (rope_vec_ok<KeyT, CacheT>(p)) {
+    p.div_half = FastDiv(static_cast<uint32_t>(p.rot_dim / 4));
+    if (pos_type == LMCB_DTYPE_INT64) {
+      rope_k_fused_vec2_kernel<KeyT, CacheT, int64_t><<<grid, kRopeThreads, 0, stream>>>(p);
+    } else {
+      rope_k_fused_vec2_kernel<KeyT, CacheT, int32_t><<<grid, kRopeThreads, 0, stream>>>(p);
+    }
+  } else if (pos_type == LMCB_DTYPE_INT64) {
     rope_k_fused_kernel<KeyT, CacheT, int64_t><<<grid, kRopeThreads, 0, stream>>>(p);
   } else {
     rope_k_fused_kernel<KeyT, CacheT, int32_t><<<grid, kRopeThreads, 0, stream>>>(p);

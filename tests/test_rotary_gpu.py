@@ -81,3 +81,26 @@ def test_out_of_range_positions_are_skipped_and_flagged():
     want = ref.rotary_embedding_k_fused(old[ok], new[ok], key[ok], hd, cache, False)
     torch.testing.assert_close(k[ok].cpu(), want, rtol=1e-5, atol=1e-5)
     assert math.isfinite(float(k.abs().max()))
+
+
+@pytest.mark.parametrize("is_neox", [True, False])
+@pytest.mark.parametrize("case", ["rot_dim_6", "misaligned_key"])
+def test_scalar_fallback_shapes(is_neox, case):
+    """Shapes the two-pair vector kernel cannot take (rot_dim not a multiple
+    of 4; a key base off its vector alignment) run the one-pair kernel, with
+    the same results."""
+    g = torch.Generator().manual_seed(9)
+    T, max_pos = 300, 512
+    if case == "rot_dim_6":
+        heads, hd, rot = 4, 6, 6
+        key = torch.randn(T, heads, hd, generator=g).to(torch.bfloat16).to(DEV)
+    else:
+        heads, hd, rot = 4, 64, 64
+        buf = torch.randn(T * heads * hd + 1, generator=g).to(torch.bfloat16).to(DEV)
+        key = buf[1:].view(T, heads, hd)  # base 2 bytes past a 4-byte boundary
+    old = torch.randint(0, max_pos, (T,), generator=g).to(DEV)
+    new = torch.randint(0, max_pos, (T,), generator=g).to(DEV)
+    cache = cos_sin_cache(max_pos, rot).to(DEV)
+    want = ref.rotary_embedding_k_fused(old, new, key.clone(), hd, cache, is_neox)
+    c_ops.rotary_embedding_k_fused(old, new, key, hd, cache, is_neox)
+    torch.testing.assert_close(key.float().cpu(), want, rtol=RTOL[torch.bfloat16], atol=1e-5)
