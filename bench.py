@@ -925,8 +925,9 @@ def run_rotary(args):
     of a c2-shaped request: 32 layers x 8192 tokens x 8 heads x 128 bf16 (512
     MiB, one call over all rows, as the op is per token), moved from positions
     0..8191 to 4096..12287, neox layout, fp32 cos/sin cache of 32768
-    positions. GB/s of algorithmic HBM bytes (K read and written, two cache
-    rows and two positions per token) against the copy roofline."""
+    positions. GB/s of algorithmic HBM bytes (K read and written, each
+    distinct cos/sin row once, two positions per token) against the copy
+    roofline."""
     from lmcache_b200 import c_ops
 
     dev = torch.device("cuda", 0)
@@ -940,7 +941,10 @@ def run_rotary(args):
     freqs = torch.outer(torch.arange(max_pos, dtype=torch.float64), inv)
     cache = torch.cat([freqs.cos(), freqs.sin()], dim=-1).to(torch.float32).to(dev)
     n = L * T
-    alg = 2 * key.numel() * key.element_size() + n * 2 * hd * 4 + n * 2 * 8
+    # K read and written, each distinct cos/sin row read once (positions repeat
+    # across layers, so the per-token re-reads hit L2), both positions read.
+    distinct_rows = int(torch.unique(torch.cat([old, new])).numel())
+    alg = 2 * key.numel() * key.element_size() + distinct_rows * hd * 4 + n * 2 * 8
     for _ in range(args.warmup):
         c_ops.rotary_embedding_k_fused(old, new, key, hd, cache, True)
     torch.cuda.synchronize()
