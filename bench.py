@@ -69,8 +69,9 @@ def parse_args():
                     help="timed steps of the pinned-host leg (default: --steps)")
     ap.add_argument("--cpu-budget", type=float, default=15.0,
                     help="seconds of CPU work for the CPU baseline sample")
-    ap.add_argument("--cpu-max-blocks", type=int, default=1024,
-                    help="paged blocks per layer of the host-resident CPU baseline buffers")
+    ap.add_argument("--cpu-max-blocks", type=int, default=0,
+                    help="paged blocks per layer of the host-resident CPU baseline buffers "
+                         "(0: the workload's own count when host RAM allows)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--skip-e2e", action="store_true",
                     help="HBM leg only (kernel tuning runs; the line then has no e2e)")
@@ -266,6 +267,24 @@ def measure_pcie_concurrent(dev, stream, world: int, nbytes: int = 256 << 20,
         ms = max_over_ranks(a.elapsed_time(b), world)
         out[name] = round(world * reps * nbytes / (ms / 1e3) / 1e9, 2)
     return out
+
+
+def workload_config(spec, world: int) -> dict:
+    """The workload as both arms name it (identical keys and values)."""
+    return {
+        "workload": f"{spec.name}: {spec.description}",
+        "num_layers": spec.num_layers,
+        "kv_heads": spec.num_heads,
+        "head_dim": spec.head_size,
+        "block_size": spec.block_size,
+        "blocks_per_layer": spec.num_blocks,
+        "tokens": spec.num_tokens,
+        "chunk_tokens": spec.chunk_size,
+        "use_mla": spec.use_mla,
+        "l2": "inputs larger than L2 (each step touches 2x payload of distinct paged rows and "
+              "LMCache objects, >126 MB)",
+        "parallelism": f"{world} independent ranks (per-rank KV shard), no collective",
+    }
 
 
 def committed_traffic(kernel: str, workload: str):
@@ -593,10 +612,10 @@ def run_ours(args):
             "kind": "port",
             "sample": (f"torch index_select/index_copy_ store+retrieve of {m['chunks_per_step']} "
                        f"of {n_chunks} chunks x {m['steps']} steps ({m['seconds']:.1f} s), "
-                       f"{spec.name} per-chunk shapes, paged buffers reduced to "
-                       f"{m['blocks_per_layer']} of {m['full_blocks_per_layer']} blocks/layer "
-                       f"in host RAM"),
+                       f"{spec.name} per-chunk shapes, "
+                       + blocks_note(m["blocks_per_layer"], m["full_blocks_per_layer"])),
         }
+        del ct
 
     if rank == 0:
         traffic = committed_traffic("transfer_rows_bulk_kernel", spec.name)
@@ -613,20 +632,13 @@ def run_ours(args):
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) bf16 KV, seeded random block slot mappings)",
-            "config": {
-                "workload": f"{spec.name}: {spec.description}",
-                "num_layers": spec.num_layers,
-                "kv_heads": spec.num_heads,
-                "head_dim": spec.head_size,
-                "block_size": spec.block_size,
-                "blocks_per_layer": spec.num_blocks,
-                "tokens": spec.num_tokens,
-                "chunk_tokens": spec.chunk_size,
-                "step": "store all chunks then retrieve all chunks (one multi_layer_kv_transfer "
-                        "per chunk and direction), captured once as a CUDA graph with two chains: "
-                        "stores on one stream, chunk i's retrieve on a second stream after the "
-                        f"store of chunk i+{RETRIEVE_LAG} (no L2 reuse between a store and its "
-                        "retrieve)",
+            "config": workload_config(spec, world),
+            "step": "store all chunks then retrieve all chunks (one multi_layer_kv_transfer "
+                    "per chunk and direction), captured once as a CUDA graph with two chains: "
+                    "stores on one stream, chunk i's retrieve on a second stream after the "
+                    f"store of chunk i+{RETRIEVE_LAG} (no L2 reuse between a store and its "
+                    "retrieve)",
+            "detail": {
                 "value_single_stream": round(value_single, 2),
                 "single_stream_roofline_frac": round(frac_single, 4),
                 "value_eager": round(value_eager, 2),
@@ -634,9 +646,6 @@ def run_ours(args):
                 "value_batched": round(value_batched, 2),
                 "batched_roofline_frac": round(batched_frac, 4),
                 "payload_bytes_per_step_per_gpu": step_payload,
-                "l2": "inputs larger than L2 (each step touches 2x payload of distinct "
-                      "paged rows and LMCache objects, >126 MB)",
-                "parallelism": f"{world} independent ranks (per-rank KV shard), no collective",
             },
             "e2e": {
                 "value": round(e2e_duplex, 2),
@@ -698,9 +707,12 @@ def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    from lmcache_b200 import workloads as wl
-    from oracle.cpu_baseline import CpuTransfer
+    # Nothing of the lmcache_b200 package is imported here: the workload
+    # definitions are loaded from their file, and the line reports which of
+    # the package's native libraries ended up mapped (none).
+    from oracle.cpu_baseline import CpuTransfer, load_workloads, mapped_product_libraries
 
+    wl = load_workloads()
     spec = wl.SPECS[args.workload]
     ct = CpuTransfer(spec, max_blocks=args.cpu_max_blocks, seed=0)
     # Size one step to about 2 s of CPU work (at most the whole sequence).
@@ -715,8 +727,8 @@ def run_reference(args):
         total_t += t
     value = total_b / total_t / 1e9
     sample = (f"torch index_select/index_copy_ store+retrieve of {n} of {len(ct.chunks)} chunks "
-              f"per step, {spec.name} per-chunk shapes, paged buffers reduced to "
-              f"{ct.spec.num_blocks} of {spec.num_blocks} blocks/layer in host RAM")
+              f"per step, {spec.name} per-chunk shapes, "
+              + blocks_note(ct.spec.num_blocks, spec.num_blocks))
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -731,15 +743,22 @@ def run_reference(args):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded bf16 KV, seeded random block slot mappings)",
-        "config": {"workload": f"{spec.name}: {spec.description}",
-                   "step": "store then retrieve a bounded sample of chunks on host cores",
-                   "parallelism": "rank 0 only, host threads"},
+        "config": workload_config(spec, 1),
+        "step": "store then retrieve a bounded sample of chunks on host cores (rank 0 only, "
+                "all host threads)",
+        "product_libraries_loaded": mapped_product_libraries(),
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": ct.threads,
                          "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def blocks_note(blocks: int, full: int) -> str:
+    if blocks == full:
+        return f"full paged buffers ({full} blocks/layer, same slots as the GPU arm) in host RAM"
+    return f"paged buffers reduced to {blocks} of {full} blocks/layer in host RAM"
 
 
 def run_cachegen(args):

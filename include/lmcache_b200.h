@@ -196,7 +196,9 @@ LMCB_API int lmcb_load_and_reshape_flash_kernel(int type, int slotType, void* st
  * host-to-device DMA into a caller-provided device staging buffer, followed
  * by an HBM scatter. Same result as lmcb_multi_layer_kv_transfer_kernel with
  * page2L == 0; the staging buffer must hold the whole object
- * (kvs * numLayers * numTokensChunk * hiddenDims elements).
+ * (kvs * numLayers * numTokensChunk * hiddenDims elements). Every argument is
+ * checked before the copy is queued, so a call that returns an error leaves
+ * the staging buffer untouched.
  *   hostCacheTensor  pinned host address of the LMCache object
  *   staging          device scratch, stagingBytes long, 16-byte aligned */
 LMCB_API int lmcb_multi_layer_kv_retrieve_staged(int type, int slotType, void* stream,
@@ -246,7 +248,9 @@ LMCB_API int lmcb_multi_layer_kv_store_staged(int type, int slotType, void* stre
  * scatters overlap on the GPU (different streams, no ordering between them)
  * race on it, so order them, for example by issuing them on one stream.
  * Nothing needs to be cleared between calls: each call writes every staging
- * byte it later reads. */
+ * byte it later reads. The area's address is kept per device ordinal for the
+ * life of the process, so calling cudaDeviceReset while the library is in use
+ * is not supported. */
 LMCB_API int lmcb_multi_layer_kv_retrieve_staged_noalloc(
     int type, int slotType, void* stream, const uint64_t* pagedKVCaches,
     const void* hostCacheTensor, const void* slotmappings, int64_t hiddenDims, int32_t kvs,

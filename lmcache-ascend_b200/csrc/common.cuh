@@ -35,10 +35,25 @@ int current_sm_count();
 // Element size of an lmcb_dtype (0 if unknown).
 int dtype_size(int dtype);
 
+// Bytes of a dense [kvs, layers, tokens, hidden] object of `esz`-byte
+// elements. Returns false, leaving *out unset, when a factor is negative or
+// the product does not fit 64 bits.
+inline bool object_bytes(int64_t kvs, int64_t layers, int64_t tokens, int64_t hidden,
+                         int64_t esz, uint64_t* out) {
+  if (kvs < 0 || layers < 0 || tokens < 0 || hidden < 0 || esz < 0) return false;
+  uint64_t b = static_cast<uint64_t>(kvs);
+  for (int64_t f : {layers, tokens, hidden, esz}) {
+    if (__builtin_mul_overflow(b, static_cast<uint64_t>(f), &b)) return false;
+  }
+  *out = b;
+  return true;
+}
+
 // Device address of the current device's status word (LMCB_DEVICE_FLAG_*
 // bits). Kernels receive it as an argument and set bits with atomicOr; the
-// address is looked up once per device. Returns NULL on failure (and records
-// the error).
+// address is looked up once per device ordinal and kept for the life of the
+// process, so a cudaDeviceReset while the library is in use is not supported.
+// Returns NULL on failure (and records the error).
 unsigned int* device_status_ptr();
 
 __device__ __forceinline__ void raise_flag(unsigned int* status, unsigned int flag) {

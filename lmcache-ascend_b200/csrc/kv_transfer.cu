@@ -1162,9 +1162,12 @@ int lmcb_multi_layer_kv_store_staged(int type, int slotType, void* stream,
   }
   if (numTokensChunk <= 0 || numLayers <= 0) return LMCB_OK;
   const int64_t row = hiddenDims * esz;
-  const size_t bytes = static_cast<size_t>(kvs) * numLayers * numTokensChunk * row;
   if (hostCacheTensor == nullptr || hostCacheDevice == nullptr || staging == nullptr) {
     return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": NULL pointer.");
+  }
+  uint64_t bytes = 0;
+  if (!lmcb::object_bytes(kvs, numLayers, numTokensChunk, hiddenDims, esz, &bytes)) {
+    return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": object size overflows.");
   }
   if (stagingBytes < bytes) {
     return lmcb::fail(LMCB_ERR_CAPACITY,
@@ -1210,15 +1213,36 @@ int lmcb_multi_layer_kv_retrieve_staged(int type, int slotType, void* stream,
                                         int32_t numLayers, int64_t pageBuffSize,
                                         int32_t numTokensChunk) {
   lmcb::clear_error();
+  const char* who = "multi_layer_kv_retrieve_staged";
+  // Every argument the scatter would reject is rejected here, before the
+  // copy into the staging buffer is queued: a failed call leaves the buffer
+  // as it was.
   const int64_t esz = lmcb::dtype_size(type);
   if (esz == 0) {
-    return lmcb::fail(LMCB_ERR_UNSUPPORTED_DTYPE,
-                      "multi_layer_kv_retrieve_staged: ScalarType not supported.");
+    return lmcb::fail(LMCB_ERR_UNSUPPORTED_DTYPE, std::string(who) + ": ScalarType not supported.");
   }
-  if (numTokensChunk <= 0 || numLayers <= 0) return LMCB_OK;
-  const size_t bytes = static_cast<size_t>(kvs) * numLayers * numTokensChunk * hiddenDims * esz;
-  if (hostCacheTensor == nullptr || staging == nullptr) {
-    return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT, "multi_layer_kv_retrieve_staged: NULL pointer.");
+  if (slotType != LMCB_DTYPE_INT64 && slotType != LMCB_DTYPE_INT32) {
+    return lmcb::fail(LMCB_ERR_UNSUPPORTED_DTYPE,
+                      std::string(who) + ": slot ids must be int64 or int32.");
+  }
+  if (kvs != 1 && kvs != 2) {
+    return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": kvs must be 1 or 2.");
+  }
+  if (kvs == 2 && pageBuffSize <= 0) {
+    return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT,
+                      std::string(who) + ": page_buffer_size must be positive for K/V caches.");
+  }
+  if (hiddenDims <= 0 || numTokensChunk < 0 || numLayers < 0) {
+    return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": negative size.");
+  }
+  if (numTokensChunk == 0 || numLayers == 0) return LMCB_OK;
+  if (hostCacheTensor == nullptr || staging == nullptr || pagedKVCaches == nullptr ||
+      slotmappings == nullptr) {
+    return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": NULL pointer.");
+  }
+  uint64_t bytes = 0;
+  if (!lmcb::object_bytes(kvs, numLayers, numTokensChunk, hiddenDims, esz, &bytes)) {
+    return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": object size overflows.");
   }
   if (stagingBytes < bytes) {
     return lmcb::fail(LMCB_ERR_CAPACITY,

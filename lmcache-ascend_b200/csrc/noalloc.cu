@@ -14,7 +14,9 @@
 // the process exits. Host code cannot use the array's name as a device
 // address (in host code it names a host-side stand-in), so the device address
 // is looked up once per device with cudaGetSymbolAddress, with that device
-// current, and passed to the kernels.
+// current, and passed to the kernels. The address is kept per device ordinal
+// for the life of the process; a cudaDeviceReset while the library is in use
+// is not supported (the primary context it was looked up in is gone).
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -82,9 +84,12 @@ int lmcb_multi_layer_kv_retrieve_staged_noalloc(int type, int slotType, void* st
     return lmcb::fail(LMCB_ERR_INVALID_ARGUMENT,
                       "multi_layer_kv_retrieve_staged_noalloc: negative size.");
   }
-  const uint64_t bytes = static_cast<uint64_t>(kvs) * static_cast<uint64_t>(numLayers) *
-                         static_cast<uint64_t>(numTokensChunk) *
-                         static_cast<uint64_t>(hiddenDims) * static_cast<uint64_t>(esz);
+  // A product that does not fit 64 bits is certainly larger than the area;
+  // checking for overflow keeps a wrapped size from passing the bound.
+  uint64_t bytes = 0;
+  if (!lmcb::object_bytes(kvs, numLayers, numTokensChunk, hiddenDims, esz, &bytes)) {
+    bytes = UINT64_MAX;
+  }
   if (bytes > LMCB_NOALLOC_STAGING_BYTES) {
     return lmcb::fail(LMCB_ERR_CAPACITY,
                       "multi_layer_kv_retrieve_staged_noalloc: the object is " +

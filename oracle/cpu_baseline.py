@@ -14,11 +14,71 @@ Only the benchmark's CPU-baseline / reference legs use it.
 from __future__ import annotations
 
 import dataclasses
+import importlib.util
 import os
+import sys
 import time
 from typing import Dict, List
 
 import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+WORKLOADS_PY = os.path.join(ROOT, "lmcache-ascend_b200", "lmcache_b200", "workloads.py")
+
+
+def load_workloads():
+    """The workload definitions (shapes and seeded slot generator), loaded
+    from their file without importing the lmcache_b200 package: the package's
+    __init__ loads the CUDA extension, and the CPU legs must map none of the
+    product's native libraries."""
+    name = "_lmcb_workload_specs"
+    mod = sys.modules.get(name)
+    if mod is None:
+        spec = importlib.util.spec_from_file_location(name, WORKLOADS_PY)
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules[name] = mod  # dataclasses resolve annotations through sys.modules
+        spec.loader.exec_module(mod)
+    return mod
+
+
+def mapped_product_libraries() -> list[str]:
+    """Shared objects of the lmcache_b200 package mapped into this process."""
+    found = set()
+    try:
+        with open("/proc/self/maps") as f:
+            for line in f:
+                path = line.rstrip("\n").split(None, 5)[-1]
+                if "lmcache_b200" in path and path.endswith(".so"):
+                    found.add(os.path.relpath(path, ROOT))
+    except OSError:
+        pass
+    return sorted(found)
+
+
+def available_host_bytes() -> int:
+    try:
+        import psutil
+
+        return int(psutil.virtual_memory().available)
+    except Exception:  # pragma: no cover
+        return int(os.sysconf("SC_AVPHYS_PAGES") * os.sysconf("SC_PAGE_SIZE"))
+
+
+def fitting_blocks(spec, max_blocks: int) -> int:
+    """Blocks per layer for the host-resident buffers: ``max_blocks`` when
+    positive, else the full count when the paged buffers and objects take at
+    most half of the available host memory, else the largest power of two
+    that does (never fewer than the sequence needs)."""
+    if max_blocks > 0:
+        return min(spec.num_blocks, max_blocks)
+    budget = available_host_bytes() // 2
+    per_block = spec.num_layers * spec.kv * spec.block_size * spec.hidden * 2
+    objects = spec.num_layers * spec.kv * spec.num_tokens * spec.hidden * 2
+    if spec.num_blocks * per_block + objects <= budget:
+        return spec.num_blocks
+    need = -(-spec.num_tokens // spec.block_size)
+    blocks = 1 << max(0, ((budget - objects) // per_block).bit_length() - 1)
+    return max(min(blocks, spec.num_blocks), need)
 
 
 def host_threads() -> int:
@@ -31,26 +91,37 @@ def host_threads() -> int:
 class CpuTransfer:
     """Host-resident paged buffers + LMCache objects for one workload spec.
 
-    ``spec`` follows lmcache_b200.workloads.Spec. The number of blocks per
-    layer is reduced to ``max_blocks`` (host RAM), keeping every per-chunk
-    shape; slots are drawn for the reduced buffer with the same generator.
+    ``spec`` follows lmcache_b200/workloads.py's Spec. The number of blocks
+    per layer is ``fitting_blocks(spec, max_blocks)``: the full workload when
+    host RAM allows, else reduced, keeping every per-chunk shape; slots are
+    then drawn for the reduced buffer with the same generator. With the full
+    count the slots are exactly the GPU benchmark's.
     """
 
-    def __init__(self, spec, max_blocks: int, seed: int = 0, threads: int | None = None):
-        from lmcache_b200 import workloads as wl  # shapes and slot generator only
+    def __init__(self, spec, max_blocks: int = 0, seed: int = 0, threads: int | None = None):
+        wl = load_workloads()
 
         self.threads = threads or host_threads()
         torch.set_num_threads(self.threads)
-        blocks = min(spec.num_blocks, max_blocks)
+        blocks = fitting_blocks(spec, max_blocks)
         self.spec = dataclasses.replace(spec, num_blocks=blocks)
         self.full_blocks = spec.num_blocks
         s = self.spec
         self.slots = wl.make_slot_mapping(s, seed=seed)
         self.chunks = wl.chunks(self.slots, s.chunk_size)
+        # Seeded random bit patterns: one 64 MiB block, tiled into every layer
+        # with a per-layer XOR (the copy rate does not depend on the values,
+        # and drawing tens of GiB of random numbers would take a minute).
+        g = torch.Generator().manual_seed(seed)
+        pattern = torch.empty(32 << 20, dtype=torch.int16)
+        pattern.random_(-32768, 32767, generator=g)
         self.caches: List[torch.Tensor] = []
-        for _ in range(s.num_layers):
+        for layer in range(s.num_layers):
             t = torch.empty(s.layer_shape, dtype=torch.bfloat16)
-            t.view(torch.int16).random_(-32768, 32767)
+            flat = t.view(-1).view(torch.int16)
+            for i in range(0, flat.numel(), pattern.numel()):
+                n = min(pattern.numel(), flat.numel() - i)
+                torch.bitwise_xor(pattern[:n], layer, out=flat[i:i + n])
             self.caches.append(t)
         self.flat = [t.view(-1, s.hidden) for t in self.caches]
         self.objs = [torch.empty(s.memobj_shape(len(c)), dtype=torch.bfloat16) for c in self.chunks]

@@ -32,3 +32,6 @@ def test_reference_arm_line():
     assert cb["value"] == d["value"] and cb["kind"] in ("port", "reference") and cb["cores"] >= 1
     assert d["e2e"] == {"value": d["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
+    # the reference arm maps none of the product's native libraries
+    assert d["product_libraries_loaded"] == []
+    assert "full paged buffers" in cb["sample"]
