@@ -133,7 +133,10 @@ def test_multi_layer_kernel_use_mla(num_tokens, pin_alloc, transfer_path):
     num_layers, num_blocks, block_size, hd, chunk = 32, 1000, 64, 576, 256
     dtype = torch.bfloat16
     kv = kv_list(num_layers, num_blocks, block_size, 1, hd, dtype, seed=7 + num_tokens, mla=True)
-    slots = seeded_slots(num_blocks * block_size, num_tokens, seed=num_tokens)
+    # Skipped (-1) slots: with page_buffer_size = 0 the MLA path has no paged
+    # bound, so the skip rests on the slot's sign alone.
+    slots = seeded_slots(num_blocks * block_size, num_tokens, seed=num_tokens,
+                         n_neg=num_tokens // 16)
     slots_dev = slots.to(DEV)
     ptrs = ptrs_of(kv)
     kv_np = [bits(t) for t in kv]
@@ -158,9 +161,17 @@ def test_multi_layer_kernel_use_mla(num_tokens, pin_alloc, transfer_path):
     for obj, sc in zip(objs, torch.split(slots_dev, chunk)):
         c_ops.multi_layer_kv_transfer(obj.tensor, ptrs_new, sc, kv_new[0].device, 0, False, True)
     torch.cuda.synchronize()
+    valid = slots_dev[slots_dev >= 0]
     for a, b in zip(kv, kv_new):
         fa, fb = a.reshape(-1, hd), b.reshape(-1, hd)
-        assert torch.equal(fa[slots_dev], fb[slots_dev])
+        assert torch.equal(fa[valid], fb[valid])
+    # the whole caches, untouched rows included, equal the oracle's
+    new_np = [np.zeros_like(a) for a in kv_np]
+    for obj, sc in zip(objs, torch.split(slots, chunk)):
+        oracle.multi_layer_kv_transfer(bits(obj.tensor), new_np, sc.numpy(), 0, False, True)
+    for got, want in zip(kv_new, new_np):
+        assert np.array_equal(bits(got), want)
+    assert c_ops.device_status(torch.cuda.current_device()) == 0
     for i, obj in enumerate(objs):
         if i % 2:
             pin_alloc.free(obj)
