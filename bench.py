@@ -73,6 +73,8 @@ def parse_args():
                     help="paged blocks per layer of the host-resident CPU baseline buffers "
                          "(0: the workload's own count when host RAM allows)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-c5-leg", action="store_true",
+                    help="skip the pinned-host c5 (TP-8 shard) sub-measurement")
     ap.add_argument("--skip-e2e", action="store_true",
                     help="HBM leg only (kernel tuning runs; the line then has no e2e)")
     ap.add_argument("--blocks", type=int, default=None,
@@ -305,6 +307,63 @@ def committed_traffic(kernel: str, workload: str):
 # ---------------------------------------------------------------------------
 
 
+def pinned_host_leg(spec, dev, world, rank, steps, warmup):
+    """The two-stream pinned-host step (stores on one stream, chunk i's
+    retrieve on a second stream after the store of chunk i + RETRIEVE_LAG)
+    on every rank at once, each with its own seeded workload; returns the
+    whole-job GB/s (payload of all ranks over the slowest rank's time)."""
+    from lmcache_b200 import c_ops
+    from lmcache_b200 import workloads as wl
+    from lmcache_b200.v1.memory_management import PinMemoryAllocator
+
+    caches = wl.make_kv_caches(spec, dev, seed=rank)
+    ptrs = wl.pointer_tensor(caches, dev)
+    slots = wl.make_slot_mapping(spec, seed=rank)
+    host_chunks = [c.contiguous().pin_memory() for c in wl.chunks(slots, spec.chunk_size)]
+    dev_bufs = [torch.empty_like(c, device=dev) for c in host_chunks]
+    n = len(host_chunks)
+    obj_bytes = sum(torch.Size(spec.memobj_shape(len(c))).numel() * 2 for c in host_chunks)
+    arena = PinMemoryAllocator(obj_bytes + 256 * n + (1 << 20))
+    objs = [arena.allocate(spec.memobj_shape(len(c)), torch.bfloat16).tensor for c in host_chunks]
+    pbs = spec.page_buffer_size
+    stream = torch.cuda.current_stream()
+    side = torch.cuda.Stream(device=dev)
+    lag = min(RETRIEVE_LAG, n - 1)
+
+    def step():
+        for i in range(n + lag):
+            if i < n:
+                dev_bufs[i].copy_(host_chunks[i], non_blocking=True)
+                c_ops.multi_layer_kv_transfer(objs[i], ptrs, dev_bufs[i], dev, pbs, True,
+                                              spec.use_mla)
+            j = i - lag
+            if j >= 0:
+                side.wait_stream(stream)
+                with torch.cuda.stream(side):
+                    c_ops.multi_layer_kv_transfer(objs[j], ptrs, dev_bufs[j], dev, pbs, False,
+                                                  spec.use_mla)
+        stream.wait_stream(side)
+
+    for _ in range(max(1, min(warmup, 3))):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(a.elapsed_time(b), world)
+    payload = 2 * wl.payload_bytes(spec, slots)
+    value = sum_over_ranks(payload * steps, world) / (ms / 1e3) / 1e9
+    arena.close()
+    del caches, objs
+    torch.cuda.empty_cache()
+    return value
+
+
 def run_ours(args):
     rank, world, local = dist_setup()
     torch.cuda.set_device(local)
@@ -312,7 +371,8 @@ def run_ours(args):
 
     from lmcache_b200 import c_ops
     from lmcache_b200 import workloads as wl
-    from lmcache_b200.v1.memory_management import PinMemoryAllocator
+    from lmcache_b200.v1.gpu_connector import VLLMPagedMemGPUConnectorV2
+    from lmcache_b200.v1.memory_management import MemoryFormat, PinMemoryAllocator
 
     spec = wl.SPECS[args.workload]
     if args.blocks:
@@ -506,8 +566,10 @@ def run_ours(args):
         return
     obj_bytes = sum(torch.Size(spec.memobj_shape(len(c))).numel() * 2 for c in dev_chunks)
     arena = PinMemoryAllocator(obj_bytes + 256 * n_chunks + (1 << 20))
-    host_objs = [arena.allocate(spec.memobj_shape(len(c)), torch.bfloat16).tensor
-                 for c in dev_chunks]
+    obj_fmt = MemoryFormat.KV_MLA_FMT if spec.use_mla else MemoryFormat.KV_2LTD
+    host_mobjs = [arena.allocate(spec.memobj_shape(len(c)), torch.bfloat16, obj_fmt)
+                  for c in dev_chunks]
+    host_objs = [m.tensor for m in host_mobjs]
     slot_dev_bufs = [torch.empty_like(c) for c in dev_chunks]
 
     def step_e2e():
@@ -594,9 +656,59 @@ def run_ours(args):
     os.environ.pop("LMCB_HOST_RETRIEVE", None)
     os.environ.pop("LMCB_HOST_STORE", None)
     best_mode = max(e2e, key=e2e.get)
+
+    # The connector LMCache's engine drives (pinned-host objects, device slot
+    # mapping): per chunk (from_gpu / to_gpu, each returning once its host
+    # object holds the data, as the engine expects) and batched
+    # (batched_from_gpu / batched_to_gpu, one launch per direction).
+    conn = VLLMPagedMemGPUConnectorV2(spec.hidden, spec.num_layers, use_mla=spec.use_mla)
+    starts_c = [0]
+    for c in host_chunks:
+        starts_c.append(starts_c[-1] + len(c))
+    conn_rates = {}
+    for label in ("per_chunk", "batched"):
+        def conn_step():
+            if label == "per_chunk":
+                for i, m in enumerate(host_mobjs):
+                    conn.from_gpu(m, starts_c[i], starts_c[i + 1], kvcaches=caches,
+                                  slot_mapping=slots_dev)
+                for i, m in enumerate(host_mobjs):
+                    conn.to_gpu(m, starts_c[i], starts_c[i + 1], kvcaches=caches,
+                                slot_mapping=slots_dev)
+            else:
+                conn.batched_from_gpu(host_mobjs, starts_c[:-1], starts_c[1:], kvcaches=caches,
+                                      slot_mapping=slots_dev)
+                conn.batched_to_gpu(host_mobjs, starts_c[:-1], starts_c[1:], kvcaches=caches,
+                                    slot_mapping=slots_dev)
+        for _ in range(max(1, min(args.warmup, 3))):
+            conn_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        for _ in range(e2e_steps):
+            conn_step()
+        c1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        ms = max_over_ranks(c0.elapsed_time(c1), world)
+        conn_rates[label] = round(sum_over_ranks(step_payload * e2e_steps, world)
+                                  / (ms / 1e3) / 1e9, 2)
+    conn_rates["pointer_uploads"] = conn.pointer_uploads
     pcie = measure_pcie(dev, stream)
     pcie_all = measure_pcie_concurrent(dev, stream, world)
     pcie_duplex = measure_pcie_duplex(dev, world)
+    # The TP-8 deployment case (Llama-3-70B shard, 256-byte rows, pinned-host
+    # objects) on every rank at once, next to the main workload.
+    c5 = None
+    if spec.name != "c5" and not args.no_c5_leg:
+        c5_spec = wl.SPECS["c5"]
+        c5_value = pinned_host_leg(c5_spec, dev, world, rank, e2e_steps, args.warmup)
+        c5 = {"workload": f"c5: {c5_spec.description}",
+              "value": round(c5_value, 2), "unit": UNIT,
+              "step": "store + retrieve of every chunk, pinned-host objects, two streams "
+                      "(as e2e), all ranks at once, each with its own seeded shard",
+              "frac_of_duplex_copy_engines": round(c5_value / pcie_duplex, 4)}
 
     # ---- CPU baseline (rank 0, N = 1) -----------------------------------
     cpu = None
@@ -661,12 +773,19 @@ def run_ours(args):
                 "single_stream": round(e2e[best_mode], 2),
                 "single_stream_by_retrieve_path": {k: round(v, 2) for k, v in e2e.items()},
                 "per_direction_gbs": dir_rates,
+                "connector": {
+                    "path": "VLLMPagedMemGPUConnectorV2 with pinned-host KV_2LTD objects and "
+                            "the slot mapping in HBM: per_chunk = from_gpu then to_gpu per "
+                            "chunk (each call returns once its host object holds the data); "
+                            "batched = batched_from_gpu + batched_to_gpu (one launch each)",
+                    **conn_rates},
                 "pcie_copy_engine_gbs": pcie,
                 "pcie_copy_engine_all_ranks_gbs": pcie_all,
                 # both directions run at once: the ceiling is the copy engines
                 # running H2D and D2H together on every rank
                 "pcie_copy_engine_duplex_all_ranks_gbs": pcie_duplex,
                 "frac_of_duplex_copy_engines": round(e2e_duplex / pcie_duplex, 4),
+                "c5_tp8_shard": c5,
             },
             "roofline": {
                 "bound": "hbm",
@@ -881,19 +1000,21 @@ def run_layerwise(args):
     peak = measured_peaks()["hbm_gbs"]
     stream = torch.cuda.current_stream()
     out = {}
-    # The per-chunk calls are replayed from CUDA graphs (their GPU cost; from
-    # Python they are host-bound at ~5 us a call). The batched calls copy a
-    # per-call object table from host memory, which stream capture refuses,
-    # so they are issued eagerly: 32-80 calls a step, each longer than its
-    # host time.
-    for name, fn, launches in (("per_chunk", per_chunk, spec.num_layers * len(chunks)),
-                               ("batched", batched, spec.num_layers)):
+    # Both ways are replayed from CUDA graphs, so the figures are GPU time
+    # (from Python a call costs ~5 us of host time, per chunk or batched).
+    # The batched calls carry their object table in the kernel parameters,
+    # which is what lets them be captured. The batched calls issued eagerly
+    # are timed too (batched_eager).
+    for name, fn, launches, graphed in (
+            ("per_chunk", per_chunk, spec.num_layers * len(chunks), True),
+            ("batched", batched, spec.num_layers, True),
+            ("batched_eager", batched, spec.num_layers, False)):
         for _ in range(args.warmup):
             fn(True)
             fn(False)
         torch.cuda.synchronize()
         graphs = []
-        if name == "per_chunk":
+        if graphed:
             for direction in (True, False):
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g, capture_error_mode="thread_local"):
@@ -935,6 +1056,7 @@ def run_layerwise(args):
                                f"retrieve", "peak_hbm_gbs": peak},
         "per_chunk": out["per_chunk"],
         "batched": out["batched"],
+        "batched_eager": out["batched_eager"],
     }
     print(json.dumps(line), flush=True)
 

@@ -133,9 +133,12 @@ LMCB_API int lmcb_multi_layer_kv_transfer_unilateral_kernel(
  * holds T_i = tokenOffsets[i+1] - tokenOffsets[i] tokens whose slot ids are
  * slotmappings[slotStarts[i] ... slotStarts[i] + T_i). Per row the result is
  * that of lmcb_multi_layer_kv_transfer_kernel on each object in turn.
- *   objectPtrs, tokenOffsets ([numObjects + 1], ascending, tokenOffsets[0]
- *   = 0, tokenOffsets[numObjects] = totalTokens), slotStarts: device-readable
- *   until the launch completes (the kernel reads them)
+ *   objectPtrs, tokenOffsets ([numObjects + 1], ascending,
+ *   tokenOffsets[numObjects] - tokenOffsets[0] = totalTokens), slotStarts:
+ *   HOST arrays, read during the call. The table travels in the kernel
+ *   parameters (up to 255 objects per launch; larger batches are split into
+ *   several launches), so nothing is copied to the device before the launch
+ *   and the call can be captured in a CUDA graph.
  *   objectsOnDevice  1 if every object is device memory (the bulk-copy kernel
  *                    may then be chosen), 0 if any is host memory (zero-copy) */
 LMCB_API int lmcb_multi_layer_kv_transfer_batched_kernel(
@@ -150,8 +153,8 @@ LMCB_API int lmcb_multi_layer_kv_transfer_batched_kernel(
  * (at objectPtrs[i]) holds T_i = tokenOffsets[i+1] - tokenOffsets[i] tokens
  * with slot ids slotmappings[slotStarts[i] ... + T_i), laid out [T_i, 2,
  * hiddenDims] if tokenMajor else [2, T_i, hiddenDims]. Caches, strides and
- * bounds as in lmcb_single_layer_kv_transfer_kernel; objectsOnDevice as in
- * lmcb_multi_layer_kv_transfer_batched_kernel. */
+ * bounds as in lmcb_single_layer_kv_transfer_kernel; the object table (host
+ * arrays) and objectsOnDevice as in lmcb_multi_layer_kv_transfer_batched_kernel. */
 LMCB_API int lmcb_single_layer_kv_transfer_batched_kernel(
     int type, int slotType, void* stream, const uint64_t* objectPtrs,
     const int64_t* tokenOffsets, const int64_t* slotStarts, int32_t numObjects,

@@ -235,19 +235,6 @@ void multi_layer_kv_transfer(torch::Tensor& key_value,             // [kv, L, T,
       direction ? 1 : 0));
 }
 
-// The batched calls build their object table on the host per call and copy
-// it with cudaMemcpyAsync from a pinned buffer that is released when the call
-// returns. A CUDA graph would keep replaying that copy from the released
-// buffer, so the calls refuse stream capture instead of misbehaving later.
-void reject_capture(cudaStream_t stream, const char* who) {
-  cudaStreamCaptureStatus status = cudaStreamCaptureStatusNone;
-  const cudaError_t err = cudaStreamIsCapturing(stream, &status);
-  TORCH_CHECK(err == cudaSuccess, who, ": ", cudaGetErrorString(err));
-  TORCH_CHECK(status == cudaStreamCaptureStatusNone, who,
-              " cannot be captured in a CUDA graph (its object table is copied from host memory "
-              "each call); issue it outside stream capture");
-}
-
 // All chunks of a request in one launch (an addition to the reference
 // surface; the connector's batched_from_gpu / batched_to_gpu call it).
 // key_values[i] is a [kv, L, T_i, H] object holding slot_mapping[starts[i]:
@@ -302,7 +289,6 @@ void multi_layer_kv_transfer_batched(const std::vector<torch::Tensor>& key_value
   for (const auto& t : key_values) check_device(t, dev, "key_values");
   const c10::OptionalDeviceGuard device_guard(dev);
   cudaStream_t stream = current_stream();
-  reject_capture(stream, "multi_layer_kv_transfer_batched");
   const uint64_t* ptrs = static_cast<const uint64_t*>(get_kernel_ptr(key_value_ptrs));
   const void* slots = get_kernel_ptr(slot_mapping);
   const int64_t esz = first.element_size();
@@ -326,10 +312,9 @@ void multi_layer_kv_transfer_batched(const std::vector<torch::Tensor>& key_value
     }
   }
 
-  // Object table: [ptrs (n) | token offsets (n + 1) | slot starts (n)].
-  auto table = torch::empty({3 * n + 1},
-                            torch::TensorOptions().dtype(torch::kLong).pinned_memory(true));
-  int64_t* tab = table.data_ptr<int64_t>();
+  // Object table (host arrays; the library passes it in the kernel parameters).
+  std::vector<uint64_t> obj_ptrs(n);
+  std::vector<int64_t> offsets(n + 1), slot_starts(n);
   int64_t off = 0, staged_off = 0;
   for (int64_t i = 0; i < n; ++i) {
     const int64_t count = ends[i] - starts[i];
@@ -347,17 +332,15 @@ void multi_layer_kv_transfer_batched(const std::vector<torch::Tensor>& key_value
     } else {
       obj = get_kernel_ptr(key_values[i]);
     }
-    tab[i] = reinterpret_cast<int64_t>(obj);
-    tab[n + i] = off;
-    tab[2 * n + 1 + i] = starts[i];
+    obj_ptrs[i] = reinterpret_cast<uint64_t>(obj);
+    offsets[i] = off;
+    slot_starts[i] = starts[i];
     off += count;
   }
-  tab[2 * n] = off;
-  auto table_dev = table.to(dev, /*non_blocking=*/true);
-  const int64_t* td = table_dev.data_ptr<int64_t>();
+  offsets[n] = off;
   check_status(lmcb_multi_layer_kv_transfer_batched_kernel(
-      dtype, slot_dtype, stream, ptrs, reinterpret_cast<const uint64_t*>(td), td + n,
-      td + 2 * n + 1, static_cast<int32_t>(n), (on_device || staged) ? 1 : 0, slots, hidden,
+      dtype, slot_dtype, stream, ptrs, obj_ptrs.data(), offsets.data(), slot_starts.data(),
+      static_cast<int32_t>(n), (on_device || staged) ? 1 : 0, slots, hidden,
       kv_size, static_cast<int32_t>(num_layers), page_buffer_size, static_cast<int32_t>(total),
       direction ? 1 : 0));
 }
@@ -411,23 +394,19 @@ void single_layer_kv_transfer_batched(const std::vector<torch::Tensor>& lmc_kvs,
   const int slot_dtype = to_slot_dtype(slot_mapping.scalar_type());
   const c10::OptionalDeviceGuard device_guard(dev);
   cudaStream_t stream = current_stream();
-  reject_capture(stream, "single_layer_kv_transfer_batched");
-  auto table = torch::empty({3 * n + 1},
-                            torch::TensorOptions().dtype(torch::kLong).pinned_memory(true));
-  int64_t* tab = table.data_ptr<int64_t>();
+  std::vector<uint64_t> obj_ptrs(n);
+  std::vector<int64_t> offsets(n + 1), slot_starts(n);
   int64_t off = 0;
   for (int64_t i = 0; i < n; ++i) {
     const int64_t count = ends[i] - starts[i];
-    tab[i] = count == 0 ? 0 : reinterpret_cast<int64_t>(get_kernel_ptr(lmc_kvs[i]));
-    tab[n + i] = off;
-    tab[2 * n + 1 + i] = starts[i];
+    obj_ptrs[i] = count == 0 ? 0 : reinterpret_cast<uint64_t>(get_kernel_ptr(lmc_kvs[i]));
+    offsets[i] = off;
+    slot_starts[i] = starts[i];
     off += count;
   }
-  tab[2 * n] = off;
-  auto table_dev = table.to(dev, /*non_blocking=*/true);
-  const int64_t* td = table_dev.data_ptr<int64_t>();
+  offsets[n] = off;
   check_status(lmcb_single_layer_kv_transfer_batched_kernel(
-      dtype, slot_dtype, stream, reinterpret_cast<const uint64_t*>(td), td + n, td + 2 * n + 1,
+      dtype, slot_dtype, stream, obj_ptrs.data(), offsets.data(), slot_starts.data(),
       static_cast<int32_t>(n), on_device ? 1 : 0, get_kernel_ptr(vllm_key_cache),
       get_kernel_ptr(vllm_value_cache), get_kernel_ptr(slot_mapping), hidden,
       static_cast<int32_t>(total), direction ? 1 : 0, token_major ? 1 : 0, k_stride, rows));

@@ -34,6 +34,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdlib>
 #include <cstring>
@@ -55,7 +56,7 @@ constexpr int kTargetTileBytes = 32 * 1024;
 //              (kv == 1), plus kv * page_kv_offset; one LMCache object.
 //   kDirect:   paged base = base_k (kv == 0) or base_v (kv == 1); one object.
 //   kBatched:  paged side as kPtrArray; many LMCache objects, located through
-//              the object table (see TransferParams::obj_*).
+//              the launch's ObjectTable.
 //   kBatchedDirect: paged side as kDirect (one layer); many objects.
 enum PagedMode { kPtrArray = 0, kDirect = 1, kBatched = 2, kBatchedDirect = 3 };
 
@@ -97,73 +98,73 @@ struct TransferParams {
   // final destination object (same layout as lmc); rows with a skipped slot
   // are copied from it instead of being left untouched. Null otherwise.
   const uint8_t* fallback;
-  // kBatched only. Tokens t are numbered across all objects: object i holds
-  // t in [obj_offsets[i], obj_offsets[i+1]) (num_objects + 1 prefix sums),
-  // laid out [kv, num_layers, T_i, hidden] at obj_ptrs[i], and takes its slot
-  // ids from slots[obj_slot_starts[i] + (t - obj_offsets[i])].
-  const uint64_t* obj_ptrs;
-  const int64_t* obj_offsets;
-  const int64_t* obj_slot_starts;
+  // Batched modes only: the number of objects in this launch's ObjectTable.
   int32_t num_objects;
   // Object layout: 0 = [kv, num_layers, T_i, hidden];
   //                1 = token-major [T_i, kv, hidden] (single layer).
   int32_t obj_token_major;
 };
 
-// A batched launch finds each row's object by a binary search over the token
-// offsets, about log2(num_objects) dependent probes per row. When there are
-// at most kSmemObjects objects the CTA first copies the offsets into shared
-// memory as int32 (token counts are below 2^31), so a probe costs
-// shared-memory latency instead of a dependent global load. Slot starts and
-// object pointers, read once per row, stay in global memory. 1 KB fits beside
-// every ring geometry without costing a CTA per SM.
-constexpr int kSmemObjects = 255;
+// The object table of a batched launch travels in the kernel parameters
+// (constant bank, __grid_constant__), so a launch reads no table from global
+// memory, needs no host-to-device copy before it and can be captured in a
+// CUDA graph. Tokens t are numbered across the launch's objects: object i
+// holds t in [offsets[i], offsets[i+1]), is laid out [kv, num_layers, T_i,
+// hidden] (or token-major) at ptrs[i], and takes its slot ids from
+// slots[slot_starts[i] + (t - offsets[i])]. The host splits batches of more
+// than kMaxObjects objects into several launches (5 KB of parameters each).
+constexpr int kMaxObjects = 255;
 
-// Copies the offsets into `s` (kSmemObjects + 1 int32) when they fit and
-// returns the copy, else nullptr; the caller synchronises the CTA before use.
-__device__ __forceinline__ const int32_t* stage_obj_offsets(const TransferParams& p, int32_t* s,
-                                                            int tid, int nthreads) {
-  const int n = p.num_objects;
-  if (n > kSmemObjects) return nullptr;
-  for (int i = tid; i <= n; i += nthreads) s[i] = static_cast<int32_t>(p.obj_offsets[i]);
-  return s;
+template <bool kBatched>
+struct ObjectTable {};  // non-batched launches carry no table
+
+template <>
+struct ObjectTable<true> {
+  uint64_t ptrs[kMaxObjects];        // base addresses (0 for empty objects)
+  int64_t slot_starts[kMaxObjects];  // index of each object's first slot id
+  int32_t offsets[kMaxObjects + 1];  // token prefix sums, offsets[0] = 0
+};
+
+// A row finds its object by a binary search over the token offsets, about
+// log2(num_objects) dependent probes. Each CTA first copies the offsets into
+// shared memory (1 KB), so the probes are shared-memory loads instead of
+// divergent constant-bank reads; pointers and slot starts, read once per row
+// and uniform across most warps, are read from the parameters.
+__device__ __forceinline__ void stage_obj_offsets(const TransferParams& p,
+                                                  const ObjectTable<true>& tab, int32_t* s,
+                                                  int tid, int nthreads) {
+  for (int i = tid; i <= p.num_objects; i += nthreads) s[i] = tab.offsets[i];
 }
 
 // LMCache-side row address of (kv, layer, t) and the index of t's slot id.
-// s_offsets: the staged token offsets of a batched launch, or nullptr.
+// s_offsets: the staged token offsets of a batched launch.
 template <int MODE>
-__device__ __forceinline__ uint8_t* lmc_row(const TransferParams& p, const int32_t* s_offsets,
-                                            int kv, int layer, int t, int64_t* slot_index) {
-  if (batched_mode(MODE)) {
+__device__ __forceinline__ uint8_t* lmc_row(const TransferParams& p,
+                                            const ObjectTable<batched_mode(MODE)>& tab,
+                                            const int32_t* s_offsets, int kv, int layer, int t,
+                                            int64_t* slot_index) {
+  if constexpr (batched_mode(MODE)) {
     // Last object whose first token is <= t (empty objects are skipped over).
     int lo = 0, hi = p.num_objects;  // offsets[lo] <= t < offsets[hi]
-    int64_t first, next;
-    if (s_offsets != nullptr) {
-      while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (s_offsets[mid] <= t) lo = mid; else hi = mid;
-      }
-      first = s_offsets[lo];
-      next = s_offsets[lo + 1];
-    } else {
-      while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (__ldg(p.obj_offsets + mid) <= t) lo = mid; else hi = mid;
-      }
-      first = __ldg(p.obj_offsets + lo);
-      next = __ldg(p.obj_offsets + lo + 1);
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (s_offsets[mid] <= t) lo = mid; else hi = mid;
     }
-    const int64_t count = next - first;
+    const int64_t first = s_offsets[lo];
+    const int64_t count = s_offsets[lo + 1] - first;
     const int64_t j = t - first;
-    *slot_index = __ldg(p.obj_slot_starts + lo) + j;
+    *slot_index = tab.slot_starts[lo] + j;
     const int64_t row = p.obj_token_major
                             ? j * p.num_kv + kv
                             : (static_cast<int64_t>(kv) * p.num_layers + layer) * count + j;
-    return reinterpret_cast<uint8_t*>(__ldg(p.obj_ptrs + lo)) + row * p.row_bytes;
+    return reinterpret_cast<uint8_t*>(tab.ptrs[lo]) + row * p.row_bytes;
+  } else {
+    (void)tab;
+    (void)s_offsets;
+    *slot_index = t;
+    return p.lmc + kv * p.lmc_kv_stride + layer * p.lmc_layer_stride +
+           static_cast<int64_t>(t) * p.lmc_token_stride;
   }
-  *slot_index = t;
-  return p.lmc + kv * p.lmc_kv_stride + layer * p.lmc_layer_stride +
-         static_cast<int64_t>(t) * p.lmc_token_stride;
 }
 
 template <int VEC>
@@ -187,12 +188,13 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 
 template <typename SlotT, int VEC, int MODE>
 __global__ void __launch_bounds__(kThreads)
-transfer_rows_kernel(const TransferParams p) {
+transfer_rows_kernel(const TransferParams p,
+                     const __grid_constant__ ObjectTable<batched_mode(MODE)> tab) {
   using V = typename VecType<VEC>::T;
   __shared__ const uint8_t* s_src[kMaxTileRows];
   __shared__ uint8_t* s_dst[kMaxTileRows];
   __shared__ int s_warp_count[kMaxTileRows / 32];
-  __shared__ int32_t s_objoff[batched_mode(MODE) ? kSmemObjects + 1 : 1];
+  __shared__ int32_t s_objoff[batched_mode(MODE) ? kMaxObjects + 1 : 1];
 
   const SlotT* __restrict__ slots = static_cast<const SlotT*>(p.slots);
   const int tid = threadIdx.x;
@@ -200,9 +202,9 @@ transfer_rows_kernel(const TransferParams p) {
   const int warp = tid >> 5;
   pdl_wait();
   pdl_launch_dependents();
-  const int32_t* obj_offsets = nullptr;
+  const int32_t* obj_offsets = s_objoff;
   if constexpr (batched_mode(MODE)) {
-    obj_offsets = stage_obj_offsets(p, s_objoff, tid, kThreads);
+    stage_obj_offsets(p, tab, s_objoff, tid, kThreads);
     __syncthreads();
   }
 
@@ -225,7 +227,7 @@ transfer_rows_kernel(const TransferParams p) {
     if (tid < n_tile) {
       const int t = t0 + tid;
       int64_t slot_index;
-      uint8_t* lmc = lmc_row<MODE>(p, obj_offsets, kv, layer, t, &slot_index);
+      uint8_t* lmc = lmc_row<MODE>(p, tab, obj_offsets, kv, layer, t, &slot_index);
       const int64_t slot = static_cast<int64_t>(slots[slot_index]);
       valid = slot >= 0;
       if (valid && p.num_paged_rows > 0 && slot >= p.num_paged_rows) {
@@ -419,7 +421,8 @@ struct BulkParams {
 
 template <typename SlotT, int MODE>
 __global__ void __launch_bounds__(32)
-transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b) {
+transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b,
+                          const __grid_constant__ ObjectTable<batched_mode(MODE)> tab) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* data = smem;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(b.stages) * b.stage_bytes);
@@ -458,9 +461,9 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b) {
   }
   __syncwarp();
 
-  // Batched modes search their object table's token offsets; they are staged
-  // in shared memory right after griddepcontrol.wait (they are an input).
-  const int32_t* obj_offsets = nullptr;
+  // Batched modes search their object table's token offsets, staged in
+  // shared memory (from the kernel parameters) before the first resolution.
+  const int32_t* obj_offsets = s_objoff;
 
   // Resolves rows [b0, b0 + n) of this CTA's range into tab_src / tab_dst
   // (0 for skipped rows). All slot ids and layer bases of the batch are
@@ -483,7 +486,7 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b) {
         const int kv = static_cast<int>(b.div_layers.div(q));
         const int layer = static_cast<int>(q - kv * b.div_layers.d);
         int64_t slot_index;
-        lmcs[j] = lmc_row<MODE>(p, obj_offsets, kv, layer, tok, &slot_index);
+        lmcs[j] = lmc_row<MODE>(p, tab, obj_offsets, kv, layer, tok, &slot_index);
         slot[j] = static_cast<int64_t>(slots[slot_index]);
         if (!paged_direct(MODE)) {
           const uint64_t* arr = kv == 0 ? p.ptrs_k : p.ptrs_v;
@@ -600,12 +603,12 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b) {
       }
     }
   }
-  pdl_wait();
-  pdl_launch_dependents();
   if constexpr (batched_mode(MODE)) {
-    obj_offsets = stage_obj_offsets(p, s_objoff, lane, 32);
+    stage_obj_offsets(p, tab, s_objoff, lane, 32);  // parameters, not an input in memory
     __syncwarp();
   }
+  pdl_wait();
+  pdl_launch_dependents();
 
   int64_t issued = 0;
   for (; issued < n_groups && issued < b.stages; ++issued) issue_load(static_cast<int>(issued));
@@ -687,7 +690,7 @@ BulkConfig bulk_config(int64_t row_bytes) {
 size_t bulk_smem_bytes(const BulkParams& b, bool batched) {
   return static_cast<size_t>(b.stages) * b.stage_bytes + kBulkMaxStages * sizeof(uint64_t) +
          kBulkMaxStages * 32 * (sizeof(uint64_t) + sizeof(uint32_t)) +
-         2 * kBatchRows * sizeof(uint64_t) + (batched ? (kSmemObjects + 1) * sizeof(int32_t) : 0);
+         2 * kBatchRows * sizeof(uint64_t) + (batched ? (kMaxObjects + 1) * sizeof(int32_t) : 0);
 }
 
 // LMCB_PDL=0 launches without the programmatic-serialization attribute.
@@ -712,24 +715,36 @@ cudaError_t launch_ex(Kernel* kernel, dim3 grid, dim3 block, size_t smem, cudaSt
   return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
+// The table argument of a launch: the batched table, or the empty one.
+template <int MODE>
+const ObjectTable<batched_mode(MODE)>& table_arg(const ObjectTable<true>* tab) {
+  static const ObjectTable<false> kNone{};
+  if constexpr (batched_mode(MODE)) {
+    return *tab;
+  } else {
+    (void)tab;
+    return kNone;
+  }
+}
+
 template <typename SlotT, int MODE>
-cudaError_t launch_bulk_mode(const TransferParams& p, const BulkParams& b, int grid,
-                             cudaStream_t stream) {
+cudaError_t launch_bulk_mode(const TransferParams& p, const BulkParams& b,
+                             const ObjectTable<true>* tab, int grid, cudaStream_t stream) {
   const size_t smem = bulk_smem_bytes(b, batched_mode(MODE));
   cudaError_t err = ensure_smem_limit<&transfer_rows_bulk_kernel<SlotT, MODE>>(smem, kBulkSmemCap);
   if (err != cudaSuccess) return err;
   return launch_ex(&transfer_rows_bulk_kernel<SlotT, MODE>, dim3(grid), dim3(32), smem, stream,
-                   p, b);
+                   p, b, table_arg<MODE>(tab));
 }
 
 template <typename SlotT>
-cudaError_t launch_bulk(const TransferParams& p, const BulkParams& b, int mode, int grid,
-                        cudaStream_t stream) {
+cudaError_t launch_bulk(const TransferParams& p, const BulkParams& b,
+                        const ObjectTable<true>* tab, int mode, int grid, cudaStream_t stream) {
   switch (mode) {
-    case kPtrArray: return launch_bulk_mode<SlotT, kPtrArray>(p, b, grid, stream);
-    case kDirect: return launch_bulk_mode<SlotT, kDirect>(p, b, grid, stream);
-    case kBatched: return launch_bulk_mode<SlotT, kBatched>(p, b, grid, stream);
-    default: return launch_bulk_mode<SlotT, kBatchedDirect>(p, b, grid, stream);
+    case kPtrArray: return launch_bulk_mode<SlotT, kPtrArray>(p, b, tab, grid, stream);
+    case kDirect: return launch_bulk_mode<SlotT, kDirect>(p, b, tab, grid, stream);
+    case kBatched: return launch_bulk_mode<SlotT, kBatched>(p, b, tab, grid, stream);
+    default: return launch_bulk_mode<SlotT, kBatchedDirect>(p, b, tab, grid, stream);
   }
 }
 
@@ -757,32 +772,32 @@ int pick_vec(std::initializer_list<uint64_t> vals) {
   return 1;
 }
 
+template <typename SlotT, int VEC, int MODE>
+cudaError_t launch_vec_mode(const TransferParams& p, const ObjectTable<true>* tab, int grid,
+                            cudaStream_t stream) {
+  return launch_ex(&transfer_rows_kernel<SlotT, VEC, MODE>, dim3(grid), dim3(kThreads), 0,
+                   stream, p, table_arg<MODE>(tab));
+}
+
 template <typename SlotT, int VEC>
-cudaError_t launch_vec(const TransferParams& p, int mode, int grid, cudaStream_t stream) {
+cudaError_t launch_vec(const TransferParams& p, const ObjectTable<true>* tab, int mode, int grid,
+                       cudaStream_t stream) {
   switch (mode) {
-    case kPtrArray:
-      return launch_ex(&transfer_rows_kernel<SlotT, VEC, kPtrArray>, dim3(grid), dim3(kThreads),
-                       0, stream, p);
-    case kDirect:
-      return launch_ex(&transfer_rows_kernel<SlotT, VEC, kDirect>, dim3(grid), dim3(kThreads), 0,
-                       stream, p);
-    case kBatched:
-      return launch_ex(&transfer_rows_kernel<SlotT, VEC, kBatched>, dim3(grid), dim3(kThreads),
-                       0, stream, p);
-    default:
-      return launch_ex(&transfer_rows_kernel<SlotT, VEC, kBatchedDirect>, dim3(grid),
-                       dim3(kThreads), 0, stream, p);
+    case kPtrArray: return launch_vec_mode<SlotT, VEC, kPtrArray>(p, tab, grid, stream);
+    case kDirect: return launch_vec_mode<SlotT, VEC, kDirect>(p, tab, grid, stream);
+    case kBatched: return launch_vec_mode<SlotT, VEC, kBatched>(p, tab, grid, stream);
+    default: return launch_vec_mode<SlotT, VEC, kBatchedDirect>(p, tab, grid, stream);
   }
 }
 
 template <typename SlotT>
-cudaError_t launch_slot(const TransferParams& p, int vec, int mode, int grid,
-                        cudaStream_t stream) {
+cudaError_t launch_slot(const TransferParams& p, const ObjectTable<true>* tab, int vec, int mode,
+                        int grid, cudaStream_t stream) {
   switch (vec) {
-    case 16: return launch_vec<SlotT, 16>(p, mode, grid, stream);
-    case 8: return launch_vec<SlotT, 8>(p, mode, grid, stream);
-    case 4: return launch_vec<SlotT, 4>(p, mode, grid, stream);
-    default: return launch_vec<SlotT, 2>(p, mode, grid, stream);
+    case 16: return launch_vec<SlotT, 16>(p, tab, mode, grid, stream);
+    case 8: return launch_vec<SlotT, 8>(p, tab, mode, grid, stream);
+    case 4: return launch_vec<SlotT, 4>(p, tab, mode, grid, stream);
+    default: return launch_vec<SlotT, 2>(p, tab, mode, grid, stream);
   }
 }
 
@@ -792,7 +807,7 @@ cudaError_t launch_slot(const TransferParams& p, int vec, int mode, int grid,
 int launch_transfer(TransferParams p, int type, int slot_type, int mode,
                     std::initializer_list<uint64_t> alignment_terms,
                     cudaStream_t stream, const char* who, bool objects_on_device = false,
-                    bool force_vector = false) {
+                    bool force_vector = false, const ObjectTable<true>* tab = nullptr) {
   const int esz = dtype_size(type);
   if (esz == 0) {
     return fail(LMCB_ERR_UNSUPPORTED_DTYPE, std::string(who) + ": ScalarType not supported.");
@@ -808,10 +823,9 @@ int launch_transfer(TransferParams p, int type, int slot_type, int mode,
   if ((!batched_mode(mode) && p.lmc == nullptr) || p.slots == nullptr) {
     return fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": NULL pointer.");
   }
-  if (batched_mode(mode) &&
-      (p.obj_ptrs == nullptr || p.obj_offsets == nullptr || p.obj_slot_starts == nullptr ||
-       p.num_objects <= 0)) {
-    return fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": NULL object table.");
+  if (batched_mode(mode) && (tab == nullptr || p.num_objects <= 0 ||
+                             p.num_objects > kMaxObjects)) {
+    return fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": bad object table.");
   }
   if (!paged_direct(mode) && (p.ptrs_k == nullptr || p.ptrs_v == nullptr)) {
     return fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": NULL pointer array.");
@@ -866,8 +880,8 @@ int launch_transfer(TransferParams p, int type, int slot_type, int mode,
     if (grid > groups) grid = groups;
     if (grid < 1) grid = 1;
     cudaError_t err = slot_type == LMCB_DTYPE_INT64
-                          ? launch_bulk<int64_t>(p, b, mode, static_cast<int>(grid), stream)
-                          : launch_bulk<int32_t>(p, b, mode, static_cast<int>(grid), stream);
+                          ? launch_bulk<int64_t>(p, b, tab, mode, static_cast<int>(grid), stream)
+                          : launch_bulk<int32_t>(p, b, tab, mode, static_cast<int>(grid), stream);
     if (err != cudaSuccess) return cuda_fail(err, who);
     return LMCB_OK;
   }
@@ -890,9 +904,53 @@ int launch_transfer(TransferParams p, int type, int slot_type, int mode,
   const int grid = static_cast<int>(p.num_tiles < max_grid ? p.num_tiles : max_grid);
 
   cudaError_t err = slot_type == LMCB_DTYPE_INT64
-                        ? launch_slot<int64_t>(p, vec, mode, grid, stream)
-                        : launch_slot<int32_t>(p, vec, mode, grid, stream);
+                        ? launch_slot<int64_t>(p, tab, vec, mode, grid, stream)
+                        : launch_slot<int32_t>(p, tab, vec, mode, grid, stream);
   if (err != cudaSuccess) return cuda_fail(err, who);
+  return LMCB_OK;
+}
+
+// Launches a batched transfer whose object table is in host memory: checks
+// the table, then issues one launch per group of at most kMaxObjects objects,
+// each carrying its part of the table (token offsets rebased to 0) in its
+// kernel parameters. `p` holds every other field.
+int launch_batched(TransferParams p, int type, int slot_type, int mode,
+                   std::initializer_list<uint64_t> alignment_terms, cudaStream_t stream,
+                   const char* who, bool objects_on_device, const uint64_t* object_ptrs,
+                   const int64_t* token_offsets, const int64_t* slot_starts, int32_t num_objects,
+                   int64_t total_tokens) {
+  if (object_ptrs == nullptr || token_offsets == nullptr || slot_starts == nullptr) {
+    return fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": NULL object table.");
+  }
+  if (token_offsets[num_objects] - token_offsets[0] != total_tokens) {
+    return fail(LMCB_ERR_INVALID_ARGUMENT,
+                std::string(who) + ": token offsets do not add up to the token count.");
+  }
+  for (int32_t i = 0; i < num_objects; ++i) {
+    if (token_offsets[i + 1] < token_offsets[i] || slot_starts[i] < 0 ||
+        (token_offsets[i + 1] > token_offsets[i] && object_ptrs[i] == 0)) {
+      return fail(LMCB_ERR_INVALID_ARGUMENT,
+                  std::string(who) + ": object " + std::to_string(i) + " is malformed.");
+    }
+  }
+  ObjectTable<true> tab;
+  for (int32_t g0 = 0; g0 < num_objects; g0 += kMaxObjects) {
+    const int32_t g1 = std::min(num_objects, g0 + kMaxObjects);
+    const int64_t base = token_offsets[g0];
+    const int64_t tokens = token_offsets[g1] - base;
+    if (tokens == 0) continue;
+    for (int32_t i = g0; i < g1; ++i) {
+      tab.ptrs[i - g0] = object_ptrs[i];
+      tab.slot_starts[i - g0] = slot_starts[i];
+      tab.offsets[i - g0] = static_cast<int32_t>(token_offsets[i] - base);
+    }
+    tab.offsets[g1 - g0] = static_cast<int32_t>(tokens);
+    p.num_objects = g1 - g0;
+    p.num_tokens = static_cast<int32_t>(tokens);
+    const int rc = launch_transfer(p, type, slot_type, mode, alignment_terms, stream, who,
+                                   objects_on_device, false, &tab);
+    if (rc != LMCB_OK) return rc;
+  }
   return LMCB_OK;
 }
 
@@ -1095,13 +1153,11 @@ int lmcb_multi_layer_kv_transfer_batched_kernel(
   p.num_kv = kvs;
   p.row_bytes = esz == 0 ? 1 : row;
   p.page2L = page2L ? 1 : 0;
-  p.obj_ptrs = objectPtrs;
-  p.obj_offsets = tokenOffsets;
-  p.obj_slot_starts = slotStarts;
-  p.num_objects = numObjects;
-  return lmcb::launch_transfer(p, type, slotType, lmcb::kBatched,
-                               {static_cast<uint64_t>(row), static_cast<uint64_t>(p.page_kv_offset)},
-                               static_cast<cudaStream_t>(stream), who, objectsOnDevice != 0);
+  return lmcb::launch_batched(
+      p, type, slotType, lmcb::kBatched,
+      {static_cast<uint64_t>(row), static_cast<uint64_t>(p.page_kv_offset)},
+      static_cast<cudaStream_t>(stream), who, objectsOnDevice != 0, objectPtrs, tokenOffsets,
+      slotStarts, numObjects, totalTokens);
 }
 
 int lmcb_single_layer_kv_transfer_batched_kernel(
@@ -1129,16 +1185,13 @@ int lmcb_single_layer_kv_transfer_batched_kernel(
   p.num_kv = 2;
   p.row_bytes = esz == 0 ? 1 : row;
   p.page2L = page2L ? 1 : 0;
-  p.obj_ptrs = objectPtrs;
-  p.obj_offsets = tokenOffsets;
-  p.obj_slot_starts = slotStarts;
-  p.num_objects = numObjects;
   p.obj_token_major = tokenMajor ? 1 : 0;
-  return lmcb::launch_transfer(
+  return lmcb::launch_batched(
       p, type, slotType, lmcb::kBatchedDirect,
       {static_cast<uint64_t>(row), reinterpret_cast<uint64_t>(keyCachePtr),
        reinterpret_cast<uint64_t>(valueCachePtr), static_cast<uint64_t>(p.paged_row_stride)},
-      static_cast<cudaStream_t>(stream), who, objectsOnDevice != 0);
+      static_cast<cudaStream_t>(stream), who, objectsOnDevice != 0, objectPtrs, tokenOffsets,
+      slotStarts, numObjects, totalTokens);
 }
 
 int lmcb_multi_layer_kv_store_staged(int type, int slotType, void* stream,

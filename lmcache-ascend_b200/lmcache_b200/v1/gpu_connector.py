@@ -5,14 +5,19 @@ CUDA counterparts of LMCache-Ascend's connectors
 instead of the Ascend module:
 
 * VLLMPagedMemGPUConnectorV2 -- non-layerwise. ``_initialize_pointers``
-  builds the per-device int64 array of per-layer KV base addresses and the
-  page buffer size exactly as npu_connector.py:24-43 does; ``from_gpu`` /
-  ``to_gpu`` move one chunk between the paged KV cache and a MemoryObj with
-  one ``multi_layer_kv_transfer`` launch (store: direction True).
+  provides the per-device int64 array of per-layer KV base addresses and the
+  page buffer size (npu_connector.py:24-43); ``from_gpu`` / ``to_gpu`` move
+  one chunk between the paged KV cache and a MemoryObj with one
+  ``multi_layer_kv_transfer`` launch (store: direction True), and
+  ``batched_from_gpu`` / ``batched_to_gpu`` move many chunks in one launch.
 * VLLMPagedMemLayerwiseGPUConnector -- layerwise generators
-  ``batched_to_gpu`` / ``batched_from_gpu`` (npu_connector.py:46-262): one
-  ``single_layer_kv_transfer`` per layer and chunk on a dedicated load / store
-  CUDA stream, optionally through a device staging buffer (``use_gpu``).
+  ``batched_to_gpu`` / ``batched_from_gpu`` (npu_connector.py:46-262): every
+  chunk of a layer in one ``single_layer_kv_transfer_batched`` launch on a
+  dedicated load / store CUDA stream, or through a device staging buffer
+  (``use_gpu``).
+* VLLMBufferLayerwiseGPUConnector -- the name the reference's buffer
+  layerwise connector has (npu_connector.py:20-21, a pass-through subclass);
+  here it is the layerwise connector with its staging buffer on.
 
 Upstream LMCache is not a dependency: the classes implement the part of the
 upstream base-class behaviour these methods rely on (constructor fields,
@@ -21,16 +26,24 @@ upstream base-class behaviour these methods rely on (constructor fields,
 
 from __future__ import annotations
 
-from typing import Dict, List, Optional, Sequence, Union
+from typing import Dict, List, Optional, Sequence, Tuple, Union
 
 import torch
 
 from .. import c_ops
-from .memory_management import MemoryObj
+from .memory_management import MemoryFormat, MemoryObj
 
-KV_2LTD = "KV_2LTD"  # [2, num_layers, num_tokens, hidden]
-KV_T2D = "KV_T2D"  # [num_tokens, 2, hidden]
-KV_MLA_FMT = "KV_MLA_FMT"  # [1, num_layers, num_tokens, hidden]
+KV_2LTD = MemoryFormat.KV_2LTD  # [2, num_layers, num_tokens, hidden]
+KV_T2D = MemoryFormat.KV_T2D  # [num_tokens, 2, hidden]
+KV_MLA_FMT = MemoryFormat.KV_MLA_FMT  # [1, num_layers, num_tokens, hidden]
+
+
+def _check_format(memory_obj: MemoryObj, want: MemoryFormat) -> None:
+    """Objects carrying metadata must be in the layout the transfer writes
+    (npu_connector.py:117 asserts KV_T2D for the layerwise path)."""
+    meta = getattr(memory_obj, "metadata", None)
+    if meta is not None and meta.fmt != want:
+        raise ValueError(f"memory object format is {meta.fmt!r}, the transfer needs {want!r}")
 
 
 class VLLMPagedMemGPUConnectorV2:
@@ -40,6 +53,14 @@ class VLLMPagedMemGPUConnectorV2:
         MLA latent width).
     :param num_layers: number of attention layers.
     :param use_mla: one latent row per token instead of K and V rows.
+    :param sync_host_objects: when a call moves data to or from an object in
+        host memory, return only once the data is there (default True). This
+        is LMCache's contract for the connector: the engine hands a stored
+        object to its storage backends right after ``from_gpu`` returns, with
+        no CUDA event to wait on, and may reuse a retrieved object after
+        ``to_gpu``. With False the calls return at once and ``last_event``
+        (a CUDA event recorded after the call's work) tells the caller when
+        the data has arrived.
     """
 
     def __init__(self, hidden_dim_size: int, num_layers: int, use_gpu: bool = False, **kwargs):
@@ -47,25 +68,40 @@ class VLLMPagedMemGPUConnectorV2:
         self.num_layers = num_layers
         self.use_gpu = use_gpu
         self.use_mla = bool(kwargs.get("use_mla", False))
+        self.sync_host_objects = bool(kwargs.get("sync_host_objects", True))
         self.kv_cache_pointers = torch.empty(num_layers, dtype=torch.int64, device="cpu",
                                              pin_memory=torch.cuda.is_available())
         self.kv_cache_pointers_on_gpu: Dict[int, torch.Tensor] = {}
+        # per device: the layer addresses its device array currently holds
+        self._pointers_held: Dict[int, Tuple[int, ...]] = {}
+        self.pointer_uploads = 0  # host-to-device copies of the address array
         self.page_buffer_size = 0
+        self.last_event: Optional[torch.cuda.Event] = None
 
     def get_shape(self, num_tokens: int) -> torch.Size:
         kv = 1 if self.use_mla else 2
         return torch.Size([kv, self.num_layers, num_tokens, self.hidden_dim_size])
 
     def _initialize_pointers(self, kv_caches: List[torch.Tensor]) -> torch.Tensor:
-        """npu_connector.py:24-43 on CUDA devices."""
-        self.kv_cache_pointers.numpy()[:] = [t.data_ptr() for t in kv_caches]
+        """The device array of per-layer base addresses and page_buffer_size
+        (npu_connector.py:24-43 on CUDA devices).
+
+        The reference copies the addresses to the device on every call, a
+        copy that waits for the stream. Here the array is copied only when
+        the set of cache addresses differs from what the device array holds
+        (in practice once: vLLM allocates its KV cache once)."""
+        ptrs = tuple(t.data_ptr() for t in kv_caches)
         device = kv_caches[0].device
         assert device.type == "cuda", "The device should be a CUDA GPU."
-        idx = device.index
+        idx = device.index if device.index is not None else torch.cuda.current_device()
         if idx not in self.kv_cache_pointers_on_gpu:
             self.kv_cache_pointers_on_gpu[idx] = torch.empty(
                 self.num_layers, dtype=torch.int64, device=device)
-        self.kv_cache_pointers_on_gpu[idx].copy_(self.kv_cache_pointers)
+        if self._pointers_held.get(idx) != ptrs:
+            self.kv_cache_pointers.numpy()[:] = ptrs
+            self.kv_cache_pointers_on_gpu[idx].copy_(self.kv_cache_pointers)
+            self._pointers_held[idx] = ptrs
+            self.pointer_uploads += 1
         if self.use_mla:
             # [num_pages, page_size, head_size] or [1, num_pages, page_size, head_size]
             self.page_buffer_size = kv_caches[0].shape[-3] * kv_caches[0].shape[-2]
@@ -84,13 +120,21 @@ class VLLMPagedMemGPUConnectorV2:
             raise ValueError("'slot_mapping' should be provided in kwargs.")
         kvcaches: List[torch.Tensor] = kwargs["kvcaches"]
         slot_mapping: torch.Tensor = kwargs["slot_mapping"]
+        _check_format(memory_obj, KV_MLA_FMT if self.use_mla else KV_2LTD)
         ptrs = self._initialize_pointers(kvcaches)
         c_ops.multi_layer_kv_transfer(memory_obj.tensor, ptrs, slot_mapping[start:end],
                                       kvcaches[0].device, self.page_buffer_size, direction,
                                       self.use_mla)
-        if not memory_obj.tensor.is_cuda:
-            # A host object must hold the data when the call returns.
-            torch.cuda.current_stream().synchronize()
+        self._finish(not memory_obj.tensor.is_cuda)
+
+    def _finish(self, host_objects: bool) -> None:
+        """Records ``last_event``; waits for it when host objects were moved
+        and sync_host_objects is set."""
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream())
+        self.last_event = ev
+        if host_objects and self.sync_host_objects:
+            ev.synchronize()
 
     def _batched(self, memory_objs: Sequence[MemoryObj], starts: Sequence[int],
                  ends: Sequence[int], direction: bool, **kwargs) -> None:
@@ -102,17 +146,18 @@ class VLLMPagedMemGPUConnectorV2:
         slot_mapping: torch.Tensor = kwargs["slot_mapping"]
         ptrs = self._initialize_pointers(kvcaches)
         # One launch per residency group (device objects / pinned host objects).
+        want = KV_MLA_FMT if self.use_mla else KV_2LTD
         groups: Dict[bool, list] = {}
         for obj, s, e in zip(memory_objs, starts, ends):
             assert obj.tensor is not None
+            _check_format(obj, want)
             groups.setdefault(obj.tensor.is_cuda, []).append((obj.tensor, int(s), int(e)))
         for items in groups.values():
             c_ops.multi_layer_kv_transfer_batched(
                 [t for t, _, _ in items], ptrs, slot_mapping, [s for _, s, _ in items],
                 [e for _, _, e in items], kvcaches[0].device, self.page_buffer_size, direction,
                 self.use_mla)
-        if False in groups:
-            torch.cuda.current_stream().synchronize()
+        self._finish(False in groups)
 
     def batched_from_gpu(self, memory_objs: Sequence[MemoryObj], starts: Sequence[int],
                          ends: Sequence[int], **kwargs) -> None:
@@ -167,6 +212,7 @@ class VLLMPagedMemLayerwiseGPUConnector:
         groups: Dict[bool, list] = {}
         for obj, s, e in zip(memory_objs_layer, starts, ends):
             assert obj.tensor is not None
+            _check_format(obj, KV_T2D)
             groups.setdefault(obj.tensor.is_cuda, []).append((obj.tensor, int(s), int(e)))
         for items in groups.values():
             c_ops.single_layer_kv_transfer_batched(
@@ -203,6 +249,7 @@ class VLLMPagedMemLayerwiseGPUConnector:
             with torch.cuda.stream(self.load_stream):
                 if self.use_gpu:
                     for start, end, memory_obj in zip(starts, ends, memory_objs_layer):
+                        _check_format(memory_obj, KV_T2D)
                         tmp[start - offset : end - offset].copy_(memory_obj.tensor,
                                                                  non_blocking=True)
                 else:
@@ -249,6 +296,7 @@ class VLLMPagedMemLayerwiseGPUConnector:
                 if self.use_gpu:
                     for start, end, memory_obj in zip(starts, ends, memory_objs_layer):
                         assert memory_obj.tensor is not None
+                        _check_format(memory_obj, KV_T2D)
                         memory_obj.tensor.copy_(tmp[start - offset : end - offset],
                                                 non_blocking=True)
                 else:
@@ -258,3 +306,12 @@ class VLLMPagedMemLayerwiseGPUConnector:
             if sync:
                 self.store_stream.synchronize()
         yield
+
+
+class VLLMBufferLayerwiseGPUConnector(VLLMPagedMemLayerwiseGPUConnector):
+    """The buffer layerwise connector (npu_connector.py:20-21 subclasses the
+    upstream class without changes): the layerwise generators with every
+    layer staged through one device buffer (``use_gpu`` on by default)."""
+
+    def __init__(self, hidden_dim_size: int, num_layers: int, use_gpu: bool = True, **kwargs):
+        super().__init__(hidden_dim_size, num_layers, use_gpu=use_gpu, **kwargs)

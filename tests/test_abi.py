@@ -3,6 +3,7 @@ symbol include/*.h declares, argument errors are reported without touching a
 GPU, and the c_ops module mirrors the reference's pybind surface
 (csrc/pybind.cpp:13-26) including its error behaviour."""
 
+import ctypes
 import glob
 import os
 import re
@@ -113,6 +114,17 @@ def test_argument_errors_need_no_gpu():
     assert lib.lmcb_multi_layer_kv_transfer_batched_kernel(
         abi.LMCB_DTYPE_BF16, abi.LMCB_DTYPE_INT64, None, 8, 8, 8, 8, -1, 1, 8, 1024, 2, 4, 16,
         4, 1) == abi.LMCB_ERR_INVALID_ARGUMENT
+    # batched transfer: the object table is host memory and checked before any
+    # launch (token offsets that do not add up, a descending range, a NULL
+    # object holding tokens)
+    ptrs = (ctypes.c_uint64 * 2)(4096, 8192)
+    starts = (ctypes.c_int64 * 2)(0, 3)
+    for offs, total in (((0, 3, 5), 4), ((0, 3, 2), 2), ((0, 3, 5), 5)):
+        o = (ctypes.c_int64 * 3)(*offs)
+        p = ptrs if offs != (0, 3, 5) or total != 5 else (ctypes.c_uint64 * 2)(4096, 0)
+        assert lib.lmcb_multi_layer_kv_transfer_batched_kernel(
+            abi.LMCB_DTYPE_BF16, abi.LMCB_DTYPE_INT64, None, 8, p, o, starts, 2, 1, 8, 1024, 2,
+            4, 16, total, 1) == abi.LMCB_ERR_INVALID_ARGUMENT, offs
     # host registry
     assert lib.lmcb_host_register(None, 16, None) == abi.LMCB_ERR_INVALID_ARGUMENT
     assert lib.lmcb_host_get_device_ptr(None) is None

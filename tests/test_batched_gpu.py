@@ -179,9 +179,9 @@ def test_single_layer_batched_matches_oracle(token_major, where, transfer_path, 
     assert c_ops.device_status(torch.cuda.current_device()) == 0
 
 
-def test_many_objects_use_the_global_table(transfer_path):
-    """More objects than the kernels stage in shared memory (255): the object
-    search falls back to the global table."""
+def test_many_objects_split_into_several_launches(transfer_path):
+    """More objects than one launch's parameter table holds (255): the library
+    splits the batch into launches of at most 255 objects each."""
     spec = wl.SPECS["c1"]
     kv = wl.make_kv_caches(spec, DEV, seed=46)
     g = torch.Generator().manual_seed(47)
@@ -213,27 +213,49 @@ def test_many_objects_use_the_global_table(transfer_path):
         assert np.array_equal(bits(a), b)
 
 
-def test_batched_refuses_stream_capture():
-    """The batched calls copy a per-call object table from host memory, so
-    they raise under CUDA graph capture instead of recording that copy."""
+def test_batched_calls_replay_from_a_cuda_graph():
+    """The object table travels in the kernel parameters, so the batched calls
+    can be captured: a graph captured once and replayed with new cache
+    contents moves the new values, identical to eager calls."""
     spec = wl.SPECS["c1"]
     kv = wl.make_kv_caches(spec, DEV, seed=48)
-    sd = wl.make_slot_mapping(spec, seed=48).to(DEV)
-    objs = [torch.zeros(spec.memobj_shape(128), dtype=torch.bfloat16, device=DEV)
-            for _ in range(2)]
+    slots = wl.make_slot_mapping(spec, seed=48)
+    sd = slots.to(DEV)
+    ranges = [(0, 100), (100, 100), (100, 256)]
+    starts, ends = [s for s, _ in ranges], [e for _, e in ranges]
+    objs = [torch.zeros(spec.memobj_shape(e - s), dtype=torch.bfloat16, device=DEV)
+            for s, e in ranges]
     ptrs = wl.pointer_tensor(kv, DEV)
+    pbs = spec.page_buffer_size
+    k, v = kv[0][0], kv[0][1]
+    lmc = [torch.zeros((e - s, 2, spec.hidden), dtype=torch.bfloat16, device=DEV)
+           for s, e in ranges]
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):  # warm-up outside capture
+        c_ops.multi_layer_kv_transfer_batched(objs, ptrs, sd, starts, ends, kv[0].device, pbs,
+                                              True, False)
+    torch.cuda.current_stream().wait_stream(side)
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
-    with pytest.raises(RuntimeError, match="cannot be captured"):
-        with torch.cuda.graph(graph):
-            c_ops.multi_layer_kv_transfer_batched(objs, ptrs, sd, [0, 128], [128, 256],
-                                                  kv[0].device, spec.page_buffer_size, True,
-                                                  False)
-    k = kv[0][0]
-    v = kv[0][1]
-    lmc = [torch.zeros((128, 2, spec.hidden), dtype=torch.bfloat16, device=DEV) for _ in range(2)]
-    graph2 = torch.cuda.CUDAGraph()
-    with pytest.raises(RuntimeError, match="cannot be captured"):
-        with torch.cuda.graph(graph2):
-            c_ops.single_layer_kv_transfer_batched(lmc, k, v, sd, [0, 128], [128, 256], True,
-                                                   True)
+    with torch.cuda.graph(graph):
+        c_ops.multi_layer_kv_transfer_batched(objs, ptrs, sd, starts, ends, kv[0].device, pbs,
+                                              True, False)
+        c_ops.single_layer_kv_transfer_batched(lmc, k, v, sd, starts, ends, True, True)
+    for seed in (49, 50):
+        g = torch.Generator(device=DEV).manual_seed(seed)
+        for t in kv:
+            t.normal_(generator=g)
+        graph.replay()
+        torch.cuda.synchronize()
+        kv_np = [bits(t) for t in kv]
+        k_np, v_np = bits(k), bits(v)
+        for obj, one, (s, e) in zip(objs, lmc, ranges):
+            want = np.zeros(obj.shape, dtype=np.int16)
+            oracle.multi_layer_kv_transfer(want, kv_np, slots[s:e].numpy(), pbs, True, False)
+            assert np.array_equal(bits(obj), want)
+            want1 = np.zeros(one.shape, dtype=np.int16)
+            oracle.single_layer_kv_transfer(want1, k_np, v_np, slots[s:e].numpy(), True, True)
+            assert np.array_equal(bits(one), want1)
+    graph.reset()
+    assert c_ops.device_status(torch.cuda.current_device()) == 0

@@ -8,10 +8,11 @@ import torch
 
 from lmcache_b200 import workloads as wl
 from lmcache_b200.v1.gpu_connector import (
+    VLLMBufferLayerwiseGPUConnector,
     VLLMPagedMemGPUConnectorV2,
     VLLMPagedMemLayerwiseGPUConnector,
 )
-from lmcache_b200.v1.memory_management import PinMemoryAllocator
+from lmcache_b200.v1.memory_management import MemoryFormat, PinMemoryAllocator
 from oracle import kv_transfer as oracle
 
 pytestmark = pytest.mark.gpu
@@ -41,7 +42,8 @@ def test_v2_connector_chunks(name, arena):
     objs = []
     for s in starts:
         e = min(s + 256, n)
-        mo = arena.allocate(conn.get_shape(e - s), torch.bfloat16)
+        fmt = MemoryFormat.KV_MLA_FMT if spec.use_mla else MemoryFormat.KV_2LTD
+        mo = arena.allocate(conn.get_shape(e - s), torch.bfloat16, fmt)
         conn.from_gpu(mo, s, e, kvcaches=kv, slot_mapping=slots_dev)
         objs.append((s, e, mo))
     assert conn.page_buffer_size == spec.page_buffer_size
@@ -73,7 +75,8 @@ def test_layerwise_round_trip(use_gpu, arena):
     slots_dev = slots.to(DEV)
     starts, ends = [0, 128], [128, 200]
     conn = VLLMPagedMemLayerwiseGPUConnector(spec.hidden, spec.num_layers, use_gpu=use_gpu)
-    objs = [[arena.allocate(conn.get_shape(e - s), torch.bfloat16) for s, e in zip(starts, ends)]
+    objs = [[arena.allocate(conn.get_shape(e - s), torch.bfloat16, MemoryFormat.KV_T2D)
+             for s, e in zip(starts, ends)]
             for _ in range(spec.num_layers)]
     gen = conn.batched_from_gpu(objs, starts, ends, kvcaches=kv, slot_mapping=slots_dev, sync=True)
     for _ in range(spec.num_layers + 1):
@@ -99,3 +102,56 @@ def test_layerwise_round_trip(use_gpu, arena):
     for row in objs:
         for mo in row:
             arena.free(mo)
+
+
+def test_v2_connector_checks_format_and_caches_pointers(arena):
+    spec = wl.SPECS["c1"]
+    kv = wl.make_kv_caches(spec, DEV, seed=10)
+    slots = wl.make_slot_mapping(spec, seed=10).to(DEV)
+    conn = VLLMPagedMemGPUConnectorV2(spec.hidden, spec.num_layers)
+    wrong = arena.allocate(conn.get_shape(256), torch.bfloat16, MemoryFormat.KV_T2D)
+    with pytest.raises(ValueError, match="format"):
+        conn.from_gpu(wrong, 0, 256, kvcaches=kv, slot_mapping=slots)
+    arena.free(wrong)
+    mo = arena.allocate(conn.get_shape(256), torch.bfloat16, MemoryFormat.KV_2LTD)
+    conn.from_gpu(mo, 0, 256, kvcaches=kv, slot_mapping=slots)
+    dev_ptrs = conn.kv_cache_pointers_on_gpu[torch.cuda.current_device()]
+    assert dev_ptrs.tolist() == [t.data_ptr() for t in kv]
+    assert conn.pointer_uploads == 1
+    # the same caches again: no new upload; other caches: one more
+    conn.from_gpu(mo, 0, 256, kvcaches=kv, slot_mapping=slots)
+    assert conn.pointer_uploads == 1
+    kv2 = [torch.zeros_like(t) for t in kv]
+    conn.to_gpu(mo, 0, 256, kvcaches=kv2, slot_mapping=slots)
+    torch.cuda.synchronize()
+    assert conn.pointer_uploads == 2
+    assert dev_ptrs.tolist() == [t.data_ptr() for t in kv2]
+    valid = slots[slots >= 0]
+    for a, b in zip(kv, kv2):
+        assert torch.equal(a.view(2, -1, spec.hidden)[:, valid], b.view(2, -1, spec.hidden)[:, valid])
+    arena.free(mo)
+
+
+def test_v2_connector_event_instead_of_sync(arena):
+    """sync_host_objects=False: calls on host objects return at once and
+    last_event marks when the data has arrived."""
+    spec = wl.SPECS["c1"]
+    kv = wl.make_kv_caches(spec, DEV, seed=11)
+    slots = wl.make_slot_mapping(spec, seed=11)
+    conn = VLLMPagedMemGPUConnectorV2(spec.hidden, spec.num_layers, sync_host_objects=False)
+    objs = [arena.allocate(conn.get_shape(128), torch.bfloat16) for _ in range(2)]
+    conn.batched_from_gpu(objs, [0, 128], [128, 256], kvcaches=kv, slot_mapping=slots.to(DEV))
+    conn.last_event.synchronize()
+    kv_np = [bits(t) for t in kv]
+    for mo, (s, e) in zip(objs, [(0, 128), (128, 256)]):
+        want = np.zeros(mo.tensor.shape, dtype=np.int16)
+        oracle.multi_layer_kv_transfer(want, kv_np, slots[s:e].numpy(), spec.page_buffer_size,
+                                       True, False)
+        assert np.array_equal(bits(mo.tensor), want)
+        arena.free(mo)
+
+
+def test_buffer_layerwise_connector_is_the_staged_layerwise_path():
+    spec = wl.SPECS["c1"]
+    conn = VLLMBufferLayerwiseGPUConnector(spec.hidden, spec.num_layers)
+    assert isinstance(conn, VLLMPagedMemLayerwiseGPUConnector) and conn.use_gpu

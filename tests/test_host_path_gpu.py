@@ -182,5 +182,5 @@ def test_pinned_allocator_reference_checks():
     for d in (d1, d2, d3, d4):
         a.free(d)
     assert a.memcheck()
-    assert isinstance(a, TensorMemoryAllocator)
+    assert isinstance(a.allocator, TensorMemoryAllocator)
     a.close()

@@ -41,6 +41,8 @@ CHUNK = 256
 
 
 def _cases():
+    if not os.path.exists(DIGESTS):  # fails when run (GPU), not at collection
+        return [{"test": "missing", "num_tokens": 0}]
     with open(DIGESTS) as f:
         return json.load(f)["cases"]
 
@@ -144,6 +146,7 @@ def _new_obj(alloc, shape):
 @pytest.mark.parametrize("case", _cases(), ids=_case_id)
 def test_reference_case_on_gpu(case, alloc):
     test = case["test"]
+    assert test != "missing", f"{DIGESTS} is missing (tests/golden/make_reference_digests.py)"
     first_h, second_h, in_digest = _inputs(test, case["seed"])
     assert in_digest == case["inputs_sha256"], "regenerated inputs differ from the reference run"
     slots_cpu = _slots(case)
