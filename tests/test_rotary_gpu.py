@@ -104,3 +104,35 @@ def test_scalar_fallback_shapes(is_neox, case):
     want = ref.rotary_embedding_k_fused(old, new, key.clone(), hd, cache, is_neox)
     c_ops.rotary_embedding_k_fused(old, new, key, hd, cache, is_neox)
     torch.testing.assert_close(key.float().cpu(), want, rtol=RTOL[torch.bfloat16], atol=1e-5)
+
+
+@pytest.mark.parametrize("is_neox", [True, False])
+@pytest.mark.parametrize("key_dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("rot", [128, 64, 24, 12])
+def test_the_three_kernels_agree_bit_for_bit(is_neox, key_dtype, rot, monkeypatch):
+    """The 16-byte vector kernel (default where aligned), the two-pair kernel
+    and the one-pair kernel do the same fp32 arithmetic per pair: forcing each
+    (LMCB_ROPE_KERNEL) gives identical bits. rot 24 and 12 leave the 16-byte
+    kernel for bf16 neox keys (it needs rot_dim % 16 == 0) and exercise the
+    fallbacks under the default choice."""
+    g = torch.Generator().manual_seed(10)
+    T, heads, hd, max_pos = 777, 4, 128, 2048
+    key = torch.randn(T, heads, hd, generator=g).to(key_dtype).to(DEV)
+    old = torch.randint(0, max_pos, (T,), generator=g).to(DEV)
+    new = torch.randint(0, max_pos, (T,), generator=g).to(DEV)
+    cache = cos_sin_cache(max_pos, rot).to(DEV)
+    outs = {}
+    for kernel in ("default", "v16", "vec2", "pair"):
+        if kernel == "default":
+            monkeypatch.delenv("LMCB_ROPE_KERNEL", raising=False)
+        else:
+            monkeypatch.setenv("LMCB_ROPE_KERNEL", kernel)
+        k = key.clone()
+        c_ops.rotary_embedding_k_fused(old, new, k, hd, cache, is_neox)
+        outs[kernel] = k
+    for kernel in ("v16", "vec2", "pair"):
+        assert torch.equal(outs[kernel], outs["default"]), kernel
+    want = ref.rotary_embedding_k_fused(old, new, key, hd, cache, is_neox)
+    torch.testing.assert_close(outs["default"].float().cpu(), want, rtol=RTOL[key_dtype],
+                               atol=1e-5)
+    assert torch.equal(outs["default"][..., rot:], key[..., rot:])
