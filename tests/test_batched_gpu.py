@@ -9,7 +9,7 @@ import torch
 from lmcache_b200 import c_ops
 from lmcache_b200 import workloads as wl
 from lmcache_b200.v1.gpu_connector import VLLMPagedMemGPUConnectorV2
-from lmcache_b200.v1.memory_management import PinMemoryAllocator
+from lmcache_b200.v1.memory_management import PinMemoryAllocator, TensorMemoryObj
 from oracle import kv_transfer as oracle
 
 pytestmark = pytest.mark.gpu
@@ -115,8 +115,8 @@ def test_connector_batched_round_trip(arena):
     for mo in objs:
         mo.tensor.zero_()  # rows of skipped slots keep these zeros
     arena.free(objs[1])
-    objs[1] = type(objs[0])(torch.zeros(conn.get_shape(100), dtype=torch.bfloat16, device=DEV),
-                            0, 0)  # one HBM object among host objects
+    objs[1] = TensorMemoryObj.wrap(  # one HBM object among host objects
+        torch.zeros(conn.get_shape(100), dtype=torch.bfloat16, device=DEV))
     conn.batched_from_gpu(objs, starts, ends, kvcaches=kv, slot_mapping=sd)
     kv_np = [bits(t) for t in kv]
     for mo, s, e in zip(objs, starts, ends):

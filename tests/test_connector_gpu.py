@@ -140,6 +140,8 @@ def test_v2_connector_event_instead_of_sync(arena):
     slots = wl.make_slot_mapping(spec, seed=11)
     conn = VLLMPagedMemGPUConnectorV2(spec.hidden, spec.num_layers, sync_host_objects=False)
     objs = [arena.allocate(conn.get_shape(128), torch.bfloat16) for _ in range(2)]
+    for mo in objs:
+        mo.tensor.zero_()  # rows of skipped slots keep these zeros
     conn.batched_from_gpu(objs, [0, 128], [128, 256], kvcaches=kv, slot_mapping=slots.to(DEV))
     conn.last_event.synchronize()
     kv_np = [bits(t) for t in kv]
