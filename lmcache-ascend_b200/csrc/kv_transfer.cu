@@ -50,6 +50,7 @@ constexpr int kThreads = 256;
 constexpr int kMaxTileRows = 128;
 constexpr int kUnroll = 4;
 constexpr int kTargetTileBytes = 32 * 1024;
+constexpr int kMinTilesPerSm = 4;
 
 // How row addresses are formed.
 //   kPtrArray: paged base = ptrs_k[layer] (kv == 0) or ptrs_v[layer]
@@ -948,6 +949,17 @@ int launch_transfer(TransferParams p, int type, int slot_type, int mode,
   while (tile_rows > 1 && tile_rows * row_vecs >= (int64_t(1) << 31)) tile_rows >>= 1;
   if (row_vecs >= (int64_t(1) << 31)) {
     return fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": row too long.");
+  }
+  // Short launches (a single layer of a request, a small chunk) would give
+  // some SMs one tile or none: smaller tiles, down to 32 rows, until every SM
+  // has about kMinTilesPerSm of them (LMCB_VEC_MIN_TILES_PER_SM overrides).
+  {
+    const int64_t want = static_cast<int64_t>(current_sm_count()) *
+                         env_int("LMCB_VEC_MIN_TILES_PER_SM", kMinTilesPerSm);
+    const int64_t seqs = static_cast<int64_t>(p.num_kv) * p.num_layers;
+    while (tile_rows > 32 && seqs * ((p.num_tokens + tile_rows - 1) / tile_rows) < want) {
+      tile_rows >>= 1;
+    }
   }
   p.tile_rows = static_cast<int32_t>(tile_rows);
   p.tiles_per_seq = static_cast<int32_t>((p.num_tokens + tile_rows - 1) / tile_rows);
