@@ -50,7 +50,7 @@ constexpr int kThreads = 256;
 constexpr int kMaxTileRows = 128;
 constexpr int kUnroll = 4;
 constexpr int kTargetTileBytes = 32 * 1024;
-constexpr int kMinTilesPerSm = 4;
+constexpr int kMinTilesPerSm = 1;
 
 // How row addresses are formed.
 //   kPtrArray: paged base = ptrs_k[layer] (kv == 0) or ptrs_v[layer]
@@ -950,9 +950,13 @@ int launch_transfer(TransferParams p, int type, int slot_type, int mode,
   if (row_vecs >= (int64_t(1) << 31)) {
     return fail(LMCB_ERR_INVALID_ARGUMENT, std::string(who) + ": row too long.");
   }
-  // Short launches (a single layer of a request, a small chunk) would give
-  // some SMs one tile or none: smaller tiles, down to 32 rows, until every SM
-  // has about kMinTilesPerSm of them (LMCB_VEC_MIN_TILES_PER_SM overrides).
+  // Tiny launches (one chunk of one layer: 512 rows) would leave most SMs
+  // without a tile: smaller tiles, down to 32 rows, until every SM has
+  // kMinTilesPerSm of them (LMCB_VEC_MIN_TILES_PER_SM overrides). Measured on
+  // B200: a c5 single-layer chunk launch 3.6 -> 2.4 us. Going further costs
+  // more than it gains: a c5 single-layer batched launch (32,768 rows of
+  // 256 B) takes 6.5 us with 128-row tiles (1.7 per SM) and 7.4 us with
+  // 64-row tiles (3.5 per SM).
   {
     const int64_t want = static_cast<int64_t>(current_sm_count()) *
                          env_int("LMCB_VEC_MIN_TILES_PER_SM", kMinTilesPerSm);
