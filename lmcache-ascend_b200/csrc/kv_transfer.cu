@@ -569,28 +569,37 @@ transfer_rows_bulk_kernel(const TransferParams p, const BulkParams b,
     }
     cur_next += count;
     const bool valid = src != nullptr;
-    const uint8_t* prev_src = reinterpret_cast<const uint8_t*>(
-        __shfl_up_sync(0xffffffffu, reinterpret_cast<uintptr_t>(src), 1));
-    uint8_t* prev_dst = reinterpret_cast<uint8_t*>(
-        __shfl_up_sync(0xffffffffu, reinterpret_cast<uintptr_t>(dst), 1));
-    const bool cont = valid && lane > 0 && prev_src != nullptr && src == prev_src + row_bytes &&
-                      dst == prev_dst + row_bytes;
-    const uint32_t cont_mask = __ballot_sync(0xffffffffu, cont);
-    const bool head = valid && !cont;
-    uint32_t run = 0;
-    if (head) {
-      // Rows lane, lane+1, ... while the following lanes continue the run.
-      const uint32_t after = lane == 31 ? 0u : (cont_mask >> (lane + 1));
-      run = 1 + static_cast<uint32_t>(__ffs(~after) - 1);
-    }
-    const uint32_t bytes = run * row_bytes;
-    const uint32_t total = __reduce_add_sync(0xffffffffu, bytes);
+    const uintptr_t prev_src =
+        __shfl_up_sync(0xffffffffu, reinterpret_cast<uintptr_t>(src), 1);
+    const uintptr_t prev_dst =
+        __shfl_up_sync(0xffffffffu, reinterpret_cast<uintptr_t>(dst), 1);
+    // Row i of the group sits in stage slot i, so rows that are consecutive
+    // on one side move with one copy on that side. The two sides merge
+    // independently: a store of random slots into an object (MLA) writes each
+    // group with one copy, a retrieve from it reads each group with one; when
+    // both sides are contiguous (consecutive slots of a page, consecutive
+    // tokens of the object) both merge.
+    const bool prev_valid = lane > 0 && prev_src != 0;
+    const bool cont_src =
+        valid && prev_valid && reinterpret_cast<uintptr_t>(src) == prev_src + row_bytes;
+    const bool cont_dst =
+        valid && prev_valid && reinterpret_cast<uintptr_t>(dst) == prev_dst + row_bytes;
+    const uint32_t src_mask = __ballot_sync(0xffffffffu, cont_src);
+    const uint32_t dst_mask = __ballot_sync(0xffffffffu, cont_dst);
+    // Rows lane, lane + 1, ... while the following lanes continue the run.
+    auto run_rows = [&](uint32_t mask) -> uint32_t {
+      const uint32_t after = lane == 31 ? 0u : (mask >> (lane + 1));
+      return 1 + static_cast<uint32_t>(__ffs(~after) - 1);
+    };
+    const uint32_t load_bytes = (valid && !cont_src) ? run_rows(src_mask) * row_bytes : 0;
+    const uint32_t store_bytes = (valid && !cont_dst) ? run_rows(dst_mask) * row_bytes : 0;
+    const uint32_t total = __reduce_add_sync(0xffffffffu, load_bytes);
     if (lane == 0) mbar_arrive_expect_tx(&bars[st], total);
     __syncwarp();
     uint8_t* stage_slot = data + static_cast<size_t>(st) * b.stage_bytes + lane * row_bytes;
-    if (bytes) bulk_load(stage_slot, src, bytes, &bars[st]);
+    if (load_bytes) bulk_load(stage_slot, src, load_bytes, &bars[st]);
     s_dst[st * 32 + lane] = reinterpret_cast<uint64_t>(dst);
-    s_len[st * 32 + lane] = bytes;
+    s_len[st * 32 + lane] = store_bytes;
   };
 
   // Under programmatic dependent launch this CTA can start while the previous
