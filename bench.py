@@ -52,10 +52,12 @@ METRIC = "KV store/retrieve GB/s (HBM & pinned-host MemoryObj)"
 # rows its own store has just left in L2, so the HBM figure is DRAM traffic.
 RETRIEVE_LAG = 4
 # The pinned-host step's lag: its objects live in host memory, so L2 reuse is
-# moot, and each chunk the retrieve stream waits at the start (and the store
-# stream idles at the end) is PCIe time with one direction idle: 32 chunks
-# with a lag of 4 keep both directions busy for at most 32 / 36 of the step.
-HOST_RETRIEVE_LAG = 1
+# moot, and every chunk the retrieve stream waits at the start (and the store
+# stream idles at the end) is PCIe time with one direction idle: a step of n
+# chunks takes about n + lag + 1 chunk times, so 32 chunks keep both
+# directions busy for 32 / 37 of the step with a lag of 4 and 32 / 33 with
+# none (each chunk's retrieve follows its own store).
+HOST_RETRIEVE_LAG = 0
 UNIT = "GB/s"
 
 
@@ -771,9 +773,9 @@ def run_ours(args):
                 "h2d_bytes_per_step": payload + sum(c.numel() * 8 for c in host_chunks),
                 "d2h_bytes_per_step": payload,
                 "path": "pinned-host MemoryObjs through c_ops, called per chunk from Python; "
-                        f"stores on one stream, chunk i's retrieve on a second stream after the "
-                        f"store of chunk i+{HOST_RETRIEVE_LAG}, so PCIe carries both directions at "
-                        "once; objects of 8 MiB "
+                        "stores on one stream, chunk i's retrieve on a second stream after the "
+                        f"store of chunk i+{HOST_RETRIEVE_LAG} (its own store when 0), so PCIe "
+                        "carries both directions at once; objects of 8 MiB "
                         "and more go through a device staging buffer and one DMA per object, "
                         "smaller ones through zero-copy kernel accesses",
                 "single_stream": round(e2e[best_mode], 2),
