@@ -104,6 +104,10 @@ struct TransferParams {
   // Object layout: 0 = [kv, num_layers, T_i, hidden];
   //                1 = token-major [T_i, kv, hidden] (single layer).
   int32_t obj_token_major;
+  // Vector kernel: 1 when this is a retrieve from device objects, whose rows
+  // each CTA prefetches into L2 for its first tile before
+  // griddepcontrol.wait (their addresses are parameters, not inputs).
+  int32_t prefetch_lmc;
 };
 
 // The object table of a batched launch travels in the kernel parameters
@@ -201,13 +205,35 @@ transfer_rows_kernel(const TransferParams p,
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
-  pdl_wait();
-  pdl_launch_dependents();
+  // The object table's offsets come from the parameters: staged before the
+  // wait, like the retrieve prefetch below.
   const int32_t* obj_offsets = s_objoff;
   if constexpr (batched_mode(MODE)) {
     stage_obj_offsets(p, tab, s_objoff, tid, kThreads);
     __syncthreads();
   }
+  // A retrieve reads object rows whose addresses come from the parameters
+  // (and the staged offsets): the CTA's first tile of them is prefetched into
+  // L2, 128-byte line by line, before the wait. A hint: if the previous kernel
+  // is still writing those lines, its writes land in L2, where the loads
+  // after the wait read them.
+  if (p.prefetch_lmc && blockIdx.x < p.num_tiles) {
+    const int64_t seq = blockIdx.x / p.tiles_per_seq;
+    const int ttile = static_cast<int>(blockIdx.x - seq * p.tiles_per_seq);
+    const int kv = static_cast<int>(seq / p.num_layers);
+    const int layer = static_cast<int>(seq - static_cast<int64_t>(kv) * p.num_layers);
+    const int t0 = ttile * p.tile_rows;
+    const int n_tile = min(p.tile_rows, p.num_tokens - t0);
+    const int lines = static_cast<int>((p.row_bytes + 127) / 128);
+    for (int i = tid; i < n_tile * lines; i += kThreads) {
+      const int r = i / lines;
+      int64_t slot_index;
+      const uint8_t* row = lmc_row<MODE>(p, tab, obj_offsets, kv, layer, t0 + r, &slot_index);
+      prefetch_l2(row + static_cast<int64_t>(i - r * lines) * 128);
+    }
+  }
+  pdl_wait();
+  pdl_launch_dependents();
 
   for (int64_t tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
     // tile -> (kv, layer, token range); token tiles vary fastest so
@@ -976,6 +1002,8 @@ int launch_transfer(TransferParams p, int type, int slot_type, int mode,
   }
   p.tile_rows = static_cast<int32_t>(tile_rows);
   p.tiles_per_seq = static_cast<int32_t>((p.num_tokens + tile_rows - 1) / tile_rows);
+  p.prefetch_lmc =
+      (!p.page2L && lmc_on_device && env_int("LMCB_BULK_PREFETCH", 1) != 0) ? 1 : 0;
   p.num_tiles = static_cast<int64_t>(p.num_kv) * p.num_layers * p.tiles_per_seq;
   p.row_vecs = FastDiv(static_cast<uint32_t>(row_vecs));
 
