@@ -48,7 +48,10 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kMaxTileRows = 128;
-constexpr int kUnroll = 4;
+// Vectors in flight per thread (all loads, then all stores): 8 x 256 threads
+// x 16 B = 32 KB, one target tile in one pass. Measured on B200: a c5
+// single-layer batched launch 5.7 us with 4, 5.2 us with 8.
+constexpr int kUnroll = 8;
 constexpr int kTargetTileBytes = 32 * 1024;
 constexpr int kMinTilesPerSm = 1;
 
