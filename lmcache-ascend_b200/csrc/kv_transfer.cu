@@ -48,10 +48,14 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kMaxTileRows = 128;
-// Vectors in flight per thread (all loads, then all stores): 8 x 256 threads
-// x 16 B = 32 KB, one target tile in one pass. Measured on B200: a c5
-// single-layer batched launch 5.7 us with 4, 5.2 us with 8.
-constexpr int kUnroll = 8;
+// Vectors in flight per thread (all loads, then all stores; a template
+// parameter of the vectorised kernel). A launch whose tiles all fit one wave
+// of CTAs takes 8 (8 x 256 threads x 16 B = 32 KB: a whole target tile in one
+// pass), longer launches 4. Measured on B200: a c5 single-layer batched
+// launch (256 tiles) 5.7 us with 4, 5.2 us with 8; a whole c2 request in one
+// launch (32,768 tiles) 0.94 of the copy roofline with 4, 0.91 with 8.
+constexpr int kUnrollShort = 8;
+constexpr int kUnrollLong = 4;
 constexpr int kTargetTileBytes = 32 * 1024;
 constexpr int kMinTilesPerSm = 1;
 
@@ -194,7 +198,7 @@ __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-template <typename SlotT, int VEC, int MODE>
+template <typename SlotT, int VEC, int MODE, int kUnroll>
 __global__ void __launch_bounds__(kThreads)
 transfer_rows_kernel(const TransferParams p,
                      const __grid_constant__ ObjectTable<batched_mode(MODE)> tab) {
@@ -856,8 +860,12 @@ int pick_vec(std::initializer_list<uint64_t> vals) {
 template <typename SlotT, int VEC, int MODE>
 cudaError_t launch_vec_mode(const TransferParams& p, const ObjectTable<true>* tab, int grid,
                             cudaStream_t stream) {
-  return launch_ex(&transfer_rows_kernel<SlotT, VEC, MODE>, dim3(grid), dim3(kThreads), 0,
-                   stream, p, table_arg<MODE>(tab));
+  if (p.num_tiles <= grid) {  // one wave: every tile has its own CTA
+    return launch_ex(&transfer_rows_kernel<SlotT, VEC, MODE, kUnrollShort>, dim3(grid),
+                     dim3(kThreads), 0, stream, p, table_arg<MODE>(tab));
+  }
+  return launch_ex(&transfer_rows_kernel<SlotT, VEC, MODE, kUnrollLong>, dim3(grid),
+                   dim3(kThreads), 0, stream, p, table_arg<MODE>(tab));
 }
 
 template <typename SlotT, int VEC>
