@@ -24,11 +24,12 @@
 //                  coder itself is sequential per stream, so both kernels are
 //                  bound by the latency of one symbol step: encode prefetches
 //                  symbols several tokens ahead, decode loads the next input
-//                  byte ahead and probes two search levels per shared-memory
-//                  round trip.
+//                  byte ahead, keeps the search's first levels in registers
+//                  and tests all probes of a round at once.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstdlib>
 #include <string>
 
 #include "common.cuh"
@@ -364,44 +365,109 @@ __device__ __forceinline__ uint32_t search_any(const uint32_t* my_cdf, uint32_t 
   return a;
 }
 
-// Alphabet of 2^D symbols: every interval of the halving search is a power
-// of two, so level k (k = D-1 .. 0) probes a + 2^k and the search unrolls
-// with no bounds tests and no branches; offsets from a are immediates. Two
-// levels share one shared-memory round trip as in search_any.
-template <int D>
-__device__ __forceinline__ uint32_t search_pow2(const uint32_t* my_cdf, uint32_t r, uint32_t x,
-                                                uint32_t& lo, uint32_t& hi) {
-  uint32_t a = 0;
-#pragma unroll
-  for (int k = D - 1; k >= 1; k -= 2) {
-    const uint32_t* row = my_cdf + a * kCoderThreads;
-    const uint32_t cm = row[(1u << k) * kCoderThreads];
-    const uint32_t c_lo = row[(1u << (k - 1)) * kCoderThreads];
-    const uint32_t c_hi = row[((1u << k) + (1u << (k - 1))) * kCoderThreads];
-    const bool ok = probe_ok(cm, r, x);
-    lo = ok ? cm : lo;
-    hi = ok ? hi : cm;
-    const uint32_t a1 = ok ? a + (1u << k) : a;
-    const uint32_t c2 = ok ? c_hi : c_lo;
-    const bool ok2 = probe_ok(c2, r, x);
-    lo = ok2 ? c2 : lo;
-    hi = ok2 ? hi : c2;
-    a = ok2 ? a1 + (1u << (k - 1)) : a1;
+// The halving search's choice inside a round of M levels whose probes
+// j = 1 .. 2^M - 1 (in units of the round's last step) were all tested at
+// once: ok[j - 1] says whether probe j was accepted. The path taken is that of
+// the one-level search: the round's first level probes 2^(M-1), and each
+// further level probes the middle of the half that the one before it kept.
+template <int M>
+__device__ __forceinline__ uint32_t pick(const bool (&ok)[(1 << M) - 1]) {
+  static_assert(M >= 1 && M <= 3, "rounds of one to three levels");
+  if constexpr (M == 1) {
+    return ok[0] ? 1u : 0u;
+  } else if constexpr (M == 2) {
+    const bool o2 = ok[1];
+    const bool o1 = o2 ? ok[2] : ok[0];
+    return (o2 ? 2u : 0u) + (o1 ? 1u : 0u);
+  } else {
+    const bool o4 = ok[3];
+    const bool o2 = o4 ? ok[5] : ok[1];
+    const bool o1 = o4 ? (o2 ? ok[6] : ok[4]) : (o2 ? ok[2] : ok[0]);
+    return (o4 ? 4u : 0u) + (o2 ? 2u : 0u) + (o1 ? 1u : 0u);
   }
-  if (D & 1) {
-    const uint32_t c1 = my_cdf[(a + 1) * kCoderThreads];
-    const bool ok = probe_ok(c1, r, x);
-    lo = ok ? c1 : lo;
-    hi = ok ? hi : c1;
-    a = ok ? a + 1 : a;
-  }
-  return a;
 }
+
+// Search over an alphabet of 2^D symbols (D >= 2) in at most three rounds,
+// each testing all probes of its levels at once:
+//   * the first R = min(D - 2, 3) levels start from a = 0, so their 2^R - 1
+//     probes are the same for every symbol and sit in registers;
+//   * the next M = D - 2 - R levels (D > 5 only) take one shared-memory round
+//     at probes a + 4j;
+//   * the last two levels load cdf[a .. a + 4] together, which also gives
+//     cdf[a] and cdf[a + 1] without tracking them through the search.
+// The probe sequence, and so the result for any CDF, is the one-level
+// search's.
+template <int D>
+struct Pow2Search {
+  static_assert(D >= 2 && D <= 8, "alphabets of 4 to 256 symbols");
+  static constexpr int R = (D - 2) < 3 ? (D - 2) : 3;
+  static constexpr int M = D - 2 - R;
+  // top[j - 1] = min(cdf[j << (D - R)], 2^15), j = 1 .. 2^R - 1.
+  uint32_t top[R > 0 ? (1 << R) - 1 : 1];
+
+  __device__ __forceinline__ void init(const uint32_t* my_cdf) {
+    if constexpr (R > 0) {
+#pragma unroll
+      for (int j = 1; j < (1 << R); ++j) {
+        const uint32_t v = my_cdf[(j << (D - R)) * kCoderThreads];
+        top[j - 1] = v < kTotal ? v : kTotal;
+        asm("" : "+r"(top[j - 1]));  // kept in a register, not reloaded per symbol
+      }
+    }
+  }
+
+  __device__ __forceinline__ uint32_t find(const uint32_t* my_cdf, uint32_t range, uint32_t r,
+                                           uint32_t x, uint32_t& lo, uint32_t& hi) const {
+    uint32_t a = 0;
+    if constexpr (R > 0) {
+      // For v <= 2^15 and r >= 1 (range >= 2^16 whenever a symbol starts),
+      // v <= min(x / r, 2^15 - 1) exactly when v * r <= min(x, 2^15 * r - 1):
+      // a value clamped to 2^15 is never accepted, as v >= 2^15 never is.
+      const uint32_t xc = min(x, (range & ~(kTotal - 1u)) - 1u);
+      bool ok[(1 << R) - 1];
+#pragma unroll
+      for (int j = 0; j < (1 << R) - 1; ++j) ok[j] = top[j] * r <= xc;
+      a = pick<R>(ok) << (D - R);
+    }
+    if constexpr (M > 0) {
+      const uint32_t* row = my_cdf + a * kCoderThreads;
+      bool ok[(1 << M) - 1];
+#pragma unroll
+      for (int j = 1; j < (1 << M); ++j) ok[j - 1] = probe_ok(row[(j << 2) * kCoderThreads], r, x);
+      a += pick<M>(ok) << 2;
+    }
+    const uint32_t* row = my_cdf + a * kCoderThreads;
+    const uint32_t c0 = row[0];
+    const uint32_t c1 = row[kCoderThreads];
+    const uint32_t c2 = row[2 * kCoderThreads];
+    const uint32_t c3 = row[3 * kCoderThreads];
+    const uint32_t c4 = row[4 * kCoderThreads];
+    const bool o2 = probe_ok(c2, r, x);
+    const bool o1 = o2 ? probe_ok(c3, r, x) : probe_ok(c1, r, x);
+    lo = o2 ? (o1 ? c3 : c2) : (o1 ? c1 : c0);
+    hi = o2 ? (o1 ? c4 : c3) : (o1 ? c2 : c1);
+    return a + (o2 ? 2u : 0u) + (o1 ? 1u : 0u);
+  }
+};
 
 // Decodes with streams either at fixed stride (ends == nullptr) or
 // concatenated with inclusive end offsets. `depth` = ceil(log2(max_bins)),
 // the most levels the halving search can take; kPow2Depth = depth when
-// max_bins is a power of two (the unrolled search), -1 otherwise.
+// max_bins is a power of two of at least 4 (the three-round search), -1
+// otherwise.
+// src[i] for i < n, else 0, as a predicated load (no branch around it).
+__device__ __forceinline__ uint32_t fetch(const uint8_t* src, int32_t i, int32_t n) {
+  uint32_t v;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.lt.s32 p, %1, %2;\n\t"
+      "mov.u32 %0, 0;\n\t"
+      "@p ld.global.nc.u8 %0, [%3];\n\t}"
+      : "=r"(v)
+      : "r"(i), "r"(n), "l"(src + i));
+  return v;
+}
+
 template <int kPow2Depth>
 __global__ void __launch_bounds__(kCoderThreads)
 decode_kernel(const uint16_t* __restrict__ cdf, const uint8_t* __restrict__ in,
@@ -437,16 +503,19 @@ decode_kernel(const uint16_t* __restrict__ cdf, const uint8_t* __restrict__ in,
     src = in + start;
     len = end - start;
   }
-  // Bytes past the stream's end read as zero. The next byte is always loaded
-  // one ahead of its use.
-  auto fetch = [&](int64_t i) -> uint32_t {
-    return i < len ? static_cast<uint32_t>(__ldg(src + i)) : 0u;
-  };
+  // Bytes past the stream's end read as zero. Positions are 32-bit: the
+  // length is clamped below 2^31 - 1 and a position stops at it (every byte
+  // from there on reads as zero), so it cannot overflow. (A symbol costs at
+  // most about 16 bits, so a stream of 2^31 bytes would hold over 2^30
+  // symbols.) The next byte is always loaded one ahead of its use.
+  const int32_t n = static_cast<int32_t>(len < INT32_MAX - 1 ? len : INT32_MAX - 1);
   uint32_t code = 0;
-  for (int i = 0; i < 4; ++i) code = (code << 8) | fetch(i);
-  int64_t pos = 4;
-  uint32_t ahead = fetch(pos);
+  for (int i = 0; i < 4; ++i) code = (code << 8) | fetch(src, i, n);
+  int32_t pos = 4;
+  uint32_t ahead = fetch(src, pos, n);
   uint32_t low = 0, range = 0xFFFFFFFFu;
+  Pow2Search<(kPow2Depth >= 2 ? kPow2Depth : 2)> pow2;
+  if constexpr (kPow2Depth >= 2) pow2.init(my_cdf);
   const uint32_t cdf_first = my_cdf[0];
   const uint32_t cdf_last = my_cdf[max_bins * kCoderThreads];
   uint8_t* dst = sym + static_cast<int64_t>(l) * T * C + c;
@@ -455,19 +524,24 @@ decode_kernel(const uint16_t* __restrict__ cdf, const uint8_t* __restrict__ in,
     const uint32_t r = range >> kProbBits;
     const uint32_t x = code - low;
     uint32_t lo = cdf_first, hi = cdf_last;
-    const uint32_t a = kPow2Depth >= 0
-                           ? search_pow2<(kPow2Depth >= 0 ? kPow2Depth : 0)>(my_cdf, r, x, lo, hi)
-                           : search_any(my_cdf, r, x, max_bins, depth, lo, hi);
+    uint32_t a;
+    if constexpr (kPow2Depth >= 2) {
+      a = pow2.find(my_cdf, range, r, x, lo, hi);
+    } else {
+      a = search_any(my_cdf, r, x, max_bins, depth, lo, hi);
+    }
     low += lo * r;
     range = r * (hi - lo);
+    // The byte-at-a-time rule with one exit test per step; the range reset
+    // is a select and the byte load is predicated, so a step has no branch
+    // but the exit (lanes of a warp renormalise on different symbols).
     for (int it = 0; it < kMaxRenorm; ++it) {
-      if ((low ^ (low + range)) >= kTop) {
-        if (range >= kBot) break;
-        range = (0u - low) & (kBot - 1u);
-      }
+      const bool unsettled = (low ^ (low + range)) >= kTop;
+      if (unsettled && range >= kBot) break;
+      range = unsettled ? ((0u - low) & (kBot - 1u)) : range;
       code = (code << 8) | ahead;
-      ++pos;
-      ahead = fetch(pos);
+      pos = min(pos + 1, n);
+      ahead = fetch(src, pos, n);
       low <<= 8;
       range <<= 8;
     }
@@ -507,10 +581,8 @@ cudaError_t launch_decode_as(const DecodeArgs& a, cudaStream_t stream) {
 
 cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream) {
   const int d = search_depth(a.max_bins);
-  if ((1 << d) != a.max_bins) return launch_decode_as<-1>(a, stream);
+  if ((1 << d) != a.max_bins || d < 2) return launch_decode_as<-1>(a, stream);
   switch (d) {
-    case 0: return launch_decode_as<0>(a, stream);
-    case 1: return launch_decode_as<1>(a, stream);
     case 2: return launch_decode_as<2>(a, stream);
     case 3: return launch_decode_as<3>(a, stream);
     case 4: return launch_decode_as<4>(a, stream);

@@ -31,6 +31,13 @@ CASES = [
     (3, 77, 33, 256),
     (1, 5, 1, 1),
     (4, 256, 96, 2),
+    # every other power-of-two alphabet (each has its own search shape)
+    (2, 300, 40, 4),
+    (1, 200, 64, 8),
+    (2, 150, 50, 64),
+    (1, 100, 20, 128),
+    # T >= 65536: calculate_cdf keeps 32-bit histogram counts
+    (1, 70000, 40, 16),
 ]
 
 
@@ -132,3 +139,38 @@ def test_decode_of_arbitrary_bytes_matches_oracle(max_bins):
     c_ops.decode_fast_prefsum(torch.from_numpy(cdf).to(DEV), torch.from_numpy(cat).to(DEV),
                               torch.from_numpy(ends).to(DEV), dec2)
     assert np.array_equal(dec2.cpu().numpy().view(np.uint8), want2)
+
+
+def wide_cdf(rng, L, C, max_bins):
+    """Strictly increasing CDF rows whose values may pass 2^15 (up to 65535):
+    probes at and above 2^15 are never accepted, and cdf[a + 1] - cdf[a] may
+    be anything from 1 up. Strictly increasing keeps every interval non-empty,
+    so the oracle's renormalisation ends."""
+    steps = rng.integers(1, 2 * 65535 // max(max_bins, 1) + 2, size=(L, C, max_bins + 1))
+    rows = np.cumsum(steps, axis=-1) - steps[..., :1] + rng.integers(0, 50, size=(L, C, 1))
+    rows = np.minimum(rows, 65535 - (max_bins - np.arange(max_bins + 1)))
+    assert (np.diff(rows, axis=-1) >= 1).all()
+    return rows.astype(np.uint16).view(np.int16)  # the int16 bit patterns c_ops takes
+
+
+@pytest.mark.parametrize("max_bins", [3, 4, 5, 8, 16, 32, 64, 128, 256])
+@pytest.mark.parametrize("kind", ["valid", "wide"])
+def test_decode_search_shapes_match_oracle(max_bins, kind):
+    """Random bytes through every search shape (alphabets of 4 to 256 symbols
+    search from registers, then in one or two shared-memory rounds; others by
+    halving with bounds tests), with CDFs from calculate_cdf or with rows that
+    pass 2^15."""
+    L, T, C = 2, 200, 67
+    rng = np.random.default_rng(1000 + max_bins)
+    if kind == "valid":
+        cdf = cg.calculate_cdf(symbols(max_bins + 7, L, T, C, max_bins), max_bins)
+    else:
+        cdf = wide_cdf(rng, L, C, max_bins)
+    cap = 80
+    streams = rng.integers(0, 256, size=(L, C, cap), dtype=np.uint8)
+    lengths = rng.integers(0, cap + 1, size=(L, C)).astype(np.int32)
+    want = cg.decode(cdf, streams, lengths, T)
+    dec = torch.zeros((L, T, C), dtype=torch.int8, device=DEV)
+    c_ops.decode_fast_new(torch.from_numpy(cdf).to(DEV), torch.from_numpy(streams).to(DEV),
+                          torch.from_numpy(lengths).to(DEV), dec)
+    assert np.array_equal(dec.cpu().numpy().view(np.uint8), want)
