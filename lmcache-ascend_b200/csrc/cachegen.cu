@@ -12,11 +12,12 @@
 //     range division is a shift on the encoder side).
 //
 // Kernels:
-//   cdf_kernel     one CTA per (layer, 32 channels): the 8 warps stream the
-//                  [T, 32] symbol tile with coalesced 32-byte row reads and
-//                  count into per-channel shared-memory histograms; then one
-//                  warp per channel scans its histogram (warp shuffle prefix
-//                  sum) and writes the channel's CDF row.
+//   cdf_kernel     one CTA per (layer, 32 channels), lane = channel: the 8
+//                  warps stream the [T, 32] symbol tile with coalesced 32-byte
+//                  row reads and count into transposed shared-memory
+//                  histograms (conflict-free atomics); then each warp scales
+//                  an eighth of the bins of every channel, and the CTA writes
+//                  its CDF rows with one coalesced copy.
 //   encode/decode  one thread per (layer, channel) stream, 32 consecutive
 //                  channels per warp so symbol reads and writes of one token
 //                  row are coalesced; the CTA's CDF rows are staged in shared
@@ -51,77 +52,111 @@ constexpr int kMaxRenorm = 16;
 
 constexpr int kCdfThreads = 256;
 constexpr int kCdfChannels = 32;
+constexpr int kCdfWarps = kCdfThreads / 32;
 
-__global__ void __launch_bounds__(kCdfThreads)
+// floor(x / n) for x < 2^46 and 0 < n < 2^31, with rn = 1.0 / n (rounded):
+// the double-precision product is within 2^-6 of x / n (relative error below
+// 2^-51), so its truncation is floor(x / n) or one off, and one exact integer
+// test each way fixes it. This replaces a 64-bit integer division (a long
+// software sequence) per CDF bin.
+__device__ __forceinline__ uint64_t div_floor(uint64_t x, uint32_t n, double rn) {
+  uint64_t q = static_cast<uint64_t>(static_cast<double>(x) * rn);
+  q = q * n > x ? q - 1 : q;
+  q = (q + 1) * n <= x ? q + 1 : q;
+  return q;
+}
+
+// Shared memory of one cdf_kernel CTA: the histograms transposed,
+// hist[bin][lane] (each lane counts into its own bank, so atomics never
+// conflict), eight per-warp partial sums per channel, and the CTA's output
+// rows [32 channels][max_bins + 1] staged for one coalesced write.
+inline size_t cdf_smem_bytes(int max_bins) {
+  return static_cast<size_t>(max_bins) * kCdfChannels * sizeof(uint32_t) +
+         static_cast<size_t>(kCdfWarps) * kCdfChannels * sizeof(uint32_t) +
+         static_cast<size_t>(kCdfChannels) * (max_bins + 1) * sizeof(uint16_t);
+}
+
+// One CTA per (layer, 32 channels), lane = channel. The eight warps count
+// interleaved token rows (32-byte coalesced row reads, four rows per warp in
+// flight) into the transposed histograms; eight CTAs per SM (32 registers a
+// thread) put a c2 chunk's 1,024 CTAs in one wave; then warp w takes the bins
+// [w * ceil(max_bins / 8), ...) of every channel, so each channel's prefix
+// sum is the warps' partial sums plus the warp's own running sum.
+__global__ void __launch_bounds__(kCdfThreads, 8)
 cdf_kernel(const uint8_t* __restrict__ sym, uint16_t* __restrict__ cdf, int T, int C,
            int max_bins, unsigned int* status) {
-  __shared__ uint32_t hist[kCdfChannels][kMaxBins + 1];
+  extern __shared__ __align__(16) uint8_t smem[];
+  uint32_t* hist = reinterpret_cast<uint32_t*>(smem);  // [max_bins][32]
+  uint32_t* part = hist + max_bins * kCdfChannels;      // [8][32]
+  uint16_t* tile = reinterpret_cast<uint16_t*>(part + kCdfWarps * kCdfChannels);
   const int l = blockIdx.y;
   const int c0 = blockIdx.x * kCdfChannels;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  constexpr int kWarps = kCdfThreads / 32;
 
-  for (int i = threadIdx.x; i < kCdfChannels * (kMaxBins + 1); i += kCdfThreads) {
-    (&hist[0][0])[i] = 0;
-  }
+  for (int i = threadIdx.x; i < max_bins * kCdfChannels; i += kCdfThreads) hist[i] = 0;
   __syncthreads();
 
   const int c = c0 + lane;
-  const uint8_t* base = sym + static_cast<int64_t>(l) * T * C;
+  const uint8_t* base = sym + static_cast<int64_t>(l) * T * C + c;
   bool oor = false;
-  if (c < C) {
-    for (int t = warp; t < T; t += kWarps) {
-      const uint32_t s = base[static_cast<int64_t>(t) * C + c];
-      if (s < static_cast<uint32_t>(max_bins)) {
-        atomicAdd(&hist[lane][s], 1u);
-      } else {
-        oor = true;
-      }
+  auto count = [&](uint32_t s) {
+    if (s < static_cast<uint32_t>(max_bins)) {
+      atomicAdd(&hist[s * kCdfChannels + lane], 1u);
+    } else {
+      oor = true;
     }
+  };
+  if (c < C) {
+    constexpr int kRows = 4;
+    int t = warp;
+    for (; t + (kRows - 1) * kCdfWarps < T; t += kRows * kCdfWarps) {
+      uint32_t v[kRows];
+#pragma unroll
+      for (int j = 0; j < kRows; ++j) v[j] = base[static_cast<int64_t>(t + j * kCdfWarps) * C];
+#pragma unroll
+      for (int j = 0; j < kRows; ++j) count(v[j]);
+    }
+    for (; t < T; t += kCdfWarps) count(base[static_cast<int64_t>(t) * C]);
   }
   if (__any_sync(0xffffffffu, oor) && lane == 0) raise_flag(status, LMCB_DEVICE_FLAG_SYMBOL_OUT_OF_RANGE);
   __syncthreads();
 
-  // One warp per channel: lane j owns bins [8j, 8j + 8).
-  for (int ch = warp; ch < kCdfChannels; ch += kWarps) {
-    const int cc = c0 + ch;
-    if (cc >= C) break;  // warp-uniform
-    uint32_t local[8];
-    uint32_t sum = 0;
+  const int per = (max_bins + kCdfWarps - 1) / kCdfWarps;
+  const int b0 = min(warp * per, max_bins);
+  const int b1 = min(b0 + per, max_bins);
+  uint32_t sum = 0;
+  for (int k = b0; k < b1; ++k) sum += hist[k * kCdfChannels + lane];
+  part[warp * kCdfChannels + lane] = sum;
+  __syncthreads();
+  uint32_t n = 0, cum = 0;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int k = lane * 8 + j;
-      local[j] = k < max_bins ? hist[ch][k] : 0u;
-      sum += local[j];
-    }
-    // Inclusive warp scan of per-lane sums.
-    uint32_t incl = sum;
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      const uint32_t v = __shfl_up_sync(0xffffffffu, incl, d);
-      if (lane >= d) incl += v;
-    }
-    const uint32_t n = __shfl_sync(0xffffffffu, incl, 31);
-    uint32_t cum = incl - sum;  // exclusive prefix = symbols below bin 8*lane
-    uint16_t* out = cdf + (static_cast<int64_t>(l) * C + cc) * (max_bins + 1);
-    const uint64_t scale = kTotal - static_cast<uint32_t>(max_bins);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int k = lane * 8 + j;
-      if (k < max_bins) {
-        uint32_t v;
-        if (n > 0) {
-          v = static_cast<uint32_t>(static_cast<uint64_t>(cum) * scale / n) + k;
-        } else {
-          v = static_cast<uint32_t>((static_cast<uint64_t>(k) * kTotal) / max_bins);
-        }
-        out[k] = static_cast<uint16_t>(v);
-      }
-      cum += local[j];
-    }
-    if (lane == 0) out[max_bins] = static_cast<uint16_t>(kTotal);
+  for (int w = 0; w < kCdfWarps; ++w) {
+    const uint32_t v = part[w * kCdfChannels + lane];
+    n += v;
+    cum += w < warp ? v : 0u;  // symbols below bin b0
   }
+  const uint64_t scale = kTotal - static_cast<uint32_t>(max_bins);
+  const double rn = n > 0 ? 1.0 / static_cast<double>(n) : 0.0;
+  uint16_t* row = tile + lane * (max_bins + 1);
+  for (int k = b0; k < b1; ++k) {
+    uint32_t v;
+    if (n > 0) {
+      v = static_cast<uint32_t>(div_floor(static_cast<uint64_t>(cum) * scale, n, rn)) + k;
+    } else {
+      v = (static_cast<uint32_t>(k) * kTotal) / static_cast<uint32_t>(max_bins);
+    }
+    row[k] = static_cast<uint16_t>(v);
+    cum += hist[k * kCdfChannels + lane];
+  }
+  if (warp == 0) row[max_bins] = static_cast<uint16_t>(kTotal);
+  __syncthreads();
+
+  // The CTA's rows are contiguous in the output.
+  const int nch = min(kCdfChannels, C - c0);
+  const int count_out = nch * (max_bins + 1);
+  uint16_t* out = cdf + (static_cast<int64_t>(l) * C + c0) * (max_bins + 1);
+  for (int i = threadIdx.x; i < count_out; i += kCdfThreads) out[i] = tile[i];
 }
 
 // ---------------------------------------------------------------------------
@@ -624,7 +659,10 @@ int lmcb_calculate_cdf(const int8_t* input, int16_t* cdfOut, int32_t numLayers, 
   unsigned int* status = lmcb::device_status_ptr();
   if (status == nullptr) return LMCB_ERR_CUDA;
   dim3 grid((numChannels + lmcb::kCdfChannels - 1) / lmcb::kCdfChannels, numLayers);
-  lmcb::cdf_kernel<<<grid, lmcb::kCdfThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+  const size_t smem = lmcb::cdf_smem_bytes(maxBins);
+  LMCB_CUDA_TRY(
+      lmcb::ensure_smem_limit<&lmcb::cdf_kernel>(smem, lmcb::cdf_smem_bytes(lmcb::kMaxBins)));
+  lmcb::cdf_kernel<<<grid, lmcb::kCdfThreads, smem, static_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const uint8_t*>(input), reinterpret_cast<uint16_t*>(cdfOut), numTokens,
       numChannels, maxBins, status);
   LMCB_CUDA_TRY(cudaGetLastError());
