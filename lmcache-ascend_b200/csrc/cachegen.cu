@@ -279,13 +279,14 @@ encode_kernel(const uint16_t* __restrict__ cdf, const uint8_t* __restrict__ sym,
   bool oor = false;
   const uint8_t* in = sym + static_cast<int64_t>(l) * T * C + c;
 
-  auto code_symbol = [&](uint32_t s) {
+  auto clamp_symbol = [&](uint32_t s) -> uint32_t {
     if (s >= static_cast<uint32_t>(max_bins)) {
       oor = true;
       s = max_bins - 1;
     }
-    const uint32_t lo = my_cdf[s * kCoderThreads];
-    const uint32_t hi = my_cdf[(s + 1) * kCoderThreads];
+    return s;
+  };
+  auto code_range = [&](uint32_t lo, uint32_t hi) {
     const uint32_t r = range >> kProbBits;
     low += lo * r;
     range = r * (hi - lo);
@@ -316,6 +317,10 @@ encode_kernel(const uint16_t* __restrict__ cdf, const uint8_t* __restrict__ sym,
       }
     }
   };
+  auto code_symbol = [&](uint32_t s) {
+    s = clamp_symbol(s);
+    code_range(my_cdf[s * kCoderThreads], my_cdf[(s + 1) * kCoderThreads]);
+  };
 
   uint32_t cur[kSymAhead];
 #pragma unroll
@@ -332,8 +337,17 @@ encode_kernel(const uint16_t* __restrict__ cdf, const uint8_t* __restrict__ sym,
       const int t = t0 + kSymAhead + j;
       nxt[j] = t < T ? static_cast<uint32_t>(__ldg(in + static_cast<int64_t>(t) * C)) : 0u;
     }
+    // The block's CDF lookups depend only on its symbols, not on the coder
+    // state, so all of them are issued before the first is used.
+    uint32_t lo[kSymAhead], hi[kSymAhead];
 #pragma unroll
-    for (int j = 0; j < kSymAhead; ++j) code_symbol(cur[j]);
+    for (int j = 0; j < kSymAhead; ++j) {
+      const uint32_t sj = clamp_symbol(cur[j]);
+      lo[j] = my_cdf[sj * kCoderThreads];
+      hi[j] = my_cdf[(sj + 1) * kCoderThreads];
+    }
+#pragma unroll
+    for (int j = 0; j < kSymAhead; ++j) code_range(lo[j], hi[j]);
 #pragma unroll
     for (int j = 0; j < kSymAhead; ++j) cur[j] = nxt[j];
   }
