@@ -36,8 +36,10 @@ CASES = [
     (1, 200, 64, 8),
     (2, 150, 50, 64),
     (1, 100, 20, 128),
-    # T >= 65536: calculate_cdf keeps 32-bit histogram counts
+    # T >= 65536
     (1, 70000, 40, 16),
+    # a ragged last group of channels with a 64-symbol alphabet
+    (2, 120, 132, 64),
 ]
 
 
@@ -103,6 +105,13 @@ def test_overflow_and_out_of_range_flags():
     c_ops.calculate_cdf(small, 4)
     torch.cuda.synchronize()
     assert c_ops.device_status(torch.cuda.current_device()) & abi.LMCB_DEVICE_FLAG_SYMBOL_OUT_OF_RANGE
+    # several channels: the out-of-range symbol is left out of its channel's counts
+    wide = np.zeros((1, 3, 8), dtype=np.uint8)
+    wide[0, 1, 5] = 9
+    cdf_w = c_ops.calculate_cdf(torch.from_numpy(wide.view(np.int8)).to(DEV), 4)
+    torch.cuda.synchronize()
+    assert c_ops.device_status(torch.cuda.current_device()) & abi.LMCB_DEVICE_FLAG_SYMBOL_OUT_OF_RANGE
+    assert np.array_equal(cdf_w.cpu().numpy(), cg.calculate_cdf(wide, 4))
 
 
 def test_empty_token_axis():
